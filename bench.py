@@ -1,0 +1,559 @@
+#!/usr/bin/env python3
+"""Benchmark of the B200 attention hot path.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload NAME] [--impl ours|reference]
+
+Default workload (decode_fp32): paged decode attention, fp32, 64 sequences with
+context ~ U[64, 2048], 8 heads x head_dim 64, 16-token blocks, block tables
+dealt from a seeded permutation of an 8192-block pool, one query token per
+sequence. A step is one decode launch over the whole batch. Metric: decode
+KV-bytes GB/s = algorithmic bytes / kernel time, where algorithmic bytes =
+sum(ctx) * kv_heads * head_dim * 2 * bytes + fp32 queries and outputs + table
+entries and context lengths. With N GPUs every rank runs its own batch (seed
+offset by rank, no collective on the data path) and value = all bytes / max
+rank time ("scaling": "weak").
+
+Other workloads: longctx_bf16 (256 sequences, context U[4096, 32768], GQA
+32/8 x 128, bf16; sequences sharded across ranks, strong scaling), prefill_f16
+(8 x 1024 causal prefill, 16 heads x 128, f16; TFLOP/s).
+
+--impl reference times the reference's own CPU kernel
+(oracle/_ref/libref.so, compiled from kernels/attention_cpu.cpp) on the same
+workload on all host cores: per sequence the page gather plus one
+inferlab_attention_forward call per q-head, as the reference worker's paged
+decode does.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+L2_FLUSH_BYTES = 256 << 20  # > 126 MB L2
+
+
+def load_peaks() -> tuple[dict, str]:
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as handle:
+            return json.load(handle), "measured"
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}, "fallback"
+
+
+def read_traffic(name: str):
+    """DRAM bytes per launch from a committed ncu summary (profiles/<name>.md,
+    line 'traffic_bytes_per_launch: N'), or None."""
+    path = os.path.join(ROOT, "profiles", f"{name}.md")
+    if not os.path.exists(path):
+        return None
+    with open(path) as handle:
+        for line in handle:
+            if line.strip().startswith("traffic_bytes_per_launch:"):
+                try:
+                    return int(float(line.split(":", 1)[1].strip()))
+                except ValueError:
+                    return None
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi samples (SM clock, throttle reasons) while the timed region runs."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_index: int):
+        self.device_id = str(device_index)
+        try:  # name the GPU by UUID so CUDA_VISIBLE_DEVICES remapping does not matter
+            import torch
+
+            uuid = str(torch.cuda.get_device_properties(device_index).uuid)
+            self.device_id = uuid if uuid.startswith("GPU-") else f"GPU-{uuid}"
+        except Exception:
+            pass
+        self.proc = None
+        self.lines: list[str] = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.device_id}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.reader = threading.Thread(target=self._read, daemon=True)
+            self.reader.start()
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            time.sleep(0.25)
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+            self.reader.join(timeout=2)
+
+    def summary(self) -> dict:
+        sms, maxes, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.lines:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sms.append(float(parts[1]))
+                maxes.append(float(parts[2]))
+            except ValueError:
+                continue
+            for name, flag in zip(names, parts[5:9]):
+                if flag.lower() == "active":
+                    reasons.add(name)
+        if not sms:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        return {"sm_mhz": statistics.median(sms), "sm_max_mhz": max(maxes),
+                "reasons": sorted(reasons), "samples": len(sms)}
+
+
+# ---------------------------------------------------------------------------
+# distributed plumbing
+# ---------------------------------------------------------------------------
+def dist_env():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+def init_dist(world: int, local: int):
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    torch.cuda.set_device(local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device(f"cuda:{local}"))
+    return dist if world > 1 else None
+
+
+def barrier(dist):
+    if dist is not None:
+        dist.barrier()
+
+
+def max_over_ranks(dist, value: float) -> float:
+    if dist is None:
+        return value
+    import torch
+
+    t = torch.tensor([value], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def sum_over_ranks(dist, value: float) -> float:
+    if dist is None:
+        return value
+    import torch
+
+    t = torch.tensor([value], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.SUM)
+    return float(t.item())
+
+
+# ---------------------------------------------------------------------------
+# workloads
+# ---------------------------------------------------------------------------
+def build_decode(workload: str, rank: int, world: int, device: int):
+    from inferlab_b200 import workloads as wl
+
+    if workload == "decode_fp32":
+        batch = wl.decode_fp32(device=device, seed=2026 + rank)
+        desc = {"workload": "paged decode fp32: 64 seqs x ctx U[64,2048], 8 heads x 64 (MHA), "
+                            "block 16, 8192-block pool, random permutation tables",
+                "num_seqs": 64, "q_heads": 8, "kv_heads": 8, "head_dim": 64,
+                "block_tokens": 16, "pool_blocks": 8192, "seed": 2026 + rank,
+                "per_rank": "independent batch per rank"}
+        return batch, desc, "f32", "weak"
+    if workload == "longctx_bf16":
+        contexts = wl.longctx_contexts(2027)
+        # greedy longest-processing-time split of sequences across ranks
+        order = np.argsort(-contexts, kind="stable")
+        loads = np.zeros(world, np.int64)
+        owner = np.zeros(len(contexts), np.int64)
+        for i in order:
+            r = int(np.argmin(loads))
+            owner[i] = r
+            loads[r] += contexts[i]
+        mine = contexts[owner == rank]
+        batch = wl.longctx_bf16(device=device, seed=2027 + rank, contexts=mine)
+        desc = {"workload": "paged decode bf16: 256 seqs x ctx U[4096,32768], GQA 32q/8kv x 128, "
+                            "block 16, sequences sharded across GPUs",
+                "num_seqs_total": 256, "num_seqs_this_rank": int(len(mine)), "q_heads": 32,
+                "kv_heads": 8, "head_dim": 128, "block_tokens": 16, "seed": 2027}
+        return batch, desc, "bf16", "strong"
+    raise SystemExit(f"unknown decode workload {workload}")
+
+
+def run_ours(args):
+    import torch
+
+    from inferlab_b200 import _lib
+
+    world, rank, local = dist_env()
+    dist = init_dist(world, local)
+    device = local
+    peaks, peak_kind = load_peaks()
+    _lib.lib()  # fails loudly if the CUDA library is missing
+
+    if args.workload == "prefill_f16":
+        return run_prefill(args, dist, world, rank, device, peaks, peak_kind)
+
+    batch, desc, dtype_name, scaling = build_decode(args.workload, rank, world, device)
+    pool = batch.pool
+    stream = torch.cuda.current_stream(device)
+    num_seqs = len(batch.contexts)
+    workspace = pool.make_workspace(num_seqs, batch.q_heads, batch.max_context_len)
+    out = torch.empty_like(batch.queries)
+    flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=f"cuda:{device}")
+    bytes_per_step = batch.decode_bytes()
+
+    def step():
+        pool.decode(batch.queries, batch.block_tables, batch.context_lens,
+                    batch.max_context_len, out=out, workspace=workspace)
+
+    for i in range(args.warmup):
+        flush.fill_(float(i))
+        step()
+    pool.synchronize()
+
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    barrier(dist)
+    torch.cuda.synchronize(device)
+    with ClockSampler(device) as clocks:
+        wall0 = time.perf_counter()
+        for i in range(args.steps):
+            flush.fill_(float(i))  # evict the previous step's K/V from L2
+            starts[i].record(stream)
+            step()
+            ends[i].record(stream)
+        torch.cuda.synchronize(device)
+        wall = time.perf_counter() - wall0
+        barrier(dist)
+    pool.synchronize()
+    kernel_ms = sum(s.elapsed_time(e) for s, e in zip(starts, ends))
+    total_ms = max_over_ranks(dist, kernel_ms)
+    all_bytes = sum_over_ranks(dist, float(bytes_per_step) * args.steps)
+    value = all_bytes / (total_ms * 1e-3) / 1e9
+    ms_per_step = total_ms / args.steps
+    achieved = bytes_per_step / (kernel_ms / args.steps * 1e-3) / 1e9
+    peak = float(peaks["hbm_gbs"])
+
+    e2e = run_decode_e2e(args, batch, pool, workspace, flush, device, dist, bytes_per_step)
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_baseline_decode(batch, bytes_per_step, args.cpu_seconds)
+
+    clock = clocks.summary()
+    line = {
+        "metric": "decode attn KV-bytes GB/s",
+        "value": round(value, 3),
+        "unit": "GB/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(ms_per_step, 5),
+        "higher_is_better": True,
+        "scaling": scaling,
+        "vs_baseline": None,
+        "dtype": dtype_name,
+        "data": "synthetic (seeded N(0,1) Q/K/V, seeded contexts and block tables)",
+        "config": dict(desc, l2="flushed between steps (256 MB write, outside the step events)",
+                       parallelism=f"sequence-sharded x{world}, no collective"),
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 2), "peak": peak, "unit": "GB/s",
+                     "frac": round(achieved / peak, 4), "peak_kind": f"{peak_kind} hbm_gbs",
+                     "traffic": read_traffic(f"paged_decode_{args.workload}"),
+                     "algorithmic_bytes_per_launch": int(bytes_per_step)},
+        "e2e": e2e,
+        "gpu_launches": args.steps,
+        "clocks": clock,
+        "wall_s_timed_region": round(wall, 4),
+    }
+    if cpu is not None:
+        line["cpu_baseline"] = cpu
+    pool.close()
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if dist is not None:
+        dist.destroy_process_group()
+
+
+def run_decode_e2e(args, batch, pool, workspace, flush, device, dist, bytes_per_step):
+    """The same step through the host-facing API with host buffers: per step,
+    copy from pinned host memory the queries, the new token's K/V rows, the
+    block tables and context lengths, append the new rows (kv_append at
+    position ctx - 1), decode, and copy the output back; host wall clock
+    around all of it (stream synchronised at the end of every step)."""
+    import torch
+
+    num_seqs, q_heads, head_dim = batch.queries.shape
+    kvh = batch.kv_heads
+    pin = dict(pin_memory=True)
+    gen = np.random.Generator(np.random.PCG64(99))
+    h_q = torch.from_numpy(gen.standard_normal((num_seqs, q_heads, head_dim), dtype=np.float32)).pin_memory()
+    h_k = torch.from_numpy(gen.standard_normal((num_seqs, kvh, head_dim), dtype=np.float32)).pin_memory()
+    h_v = torch.from_numpy(gen.standard_normal((num_seqs, kvh, head_dim), dtype=np.float32)).pin_memory()
+    h_tables = torch.from_numpy(batch.tables_host).pin_memory()
+    h_lens = torch.from_numpy(batch.contexts.astype(np.int32)).pin_memory()
+    h_pos = torch.from_numpy((batch.contexts - 1).astype(np.int32)).pin_memory()
+    h_seq = torch.arange(num_seqs, dtype=torch.int32).pin_memory()
+    h_out = torch.empty((num_seqs, q_heads, head_dim), dtype=torch.float32, **pin)
+    dev = f"cuda:{device}"
+    d_q = torch.empty_like(h_q, device=dev)
+    d_k = torch.empty_like(h_k, device=dev)
+    d_v = torch.empty_like(h_v, device=dev)
+    d_tables = torch.empty_like(h_tables, device=dev)
+    d_lens = torch.empty_like(h_lens, device=dev)
+    d_pos = torch.empty_like(h_pos, device=dev)
+    d_seq = torch.empty_like(h_seq, device=dev)
+    d_out = torch.empty_like(h_out, device=dev)
+    h2d = sum(t.numel() * t.element_size() for t in (h_q, h_k, h_v, h_tables, h_lens, h_pos, h_seq))
+    d2h = h_out.numel() * h_out.element_size()
+    stream = torch.cuda.current_stream(device)
+
+    def step():
+        for d, h in ((d_q, h_q), (d_k, h_k), (d_v, h_v), (d_tables, h_tables), (d_lens, h_lens),
+                     (d_pos, h_pos), (d_seq, h_seq)):
+            d.copy_(h, non_blocking=True)
+        pool.append(d_k, d_v, d_seq, d_pos, d_tables)
+        pool.decode(d_q, d_tables, d_lens, batch.max_context_len, out=d_out, workspace=workspace)
+        h_out.copy_(d_out, non_blocking=True)
+        stream.synchronize()
+
+    for i in range(args.warmup):
+        flush.fill_(float(i))
+        step()
+    pool.synchronize()
+    total = 0.0
+    barrier(dist)
+    for i in range(args.steps):
+        flush.fill_(float(i))
+        stream.synchronize()
+        t0 = time.perf_counter()
+        step()
+        total += time.perf_counter() - t0
+    pool.synchronize()
+    barrier(dist)
+    total = max_over_ranks(dist, total)
+    all_bytes = sum_over_ranks(dist, float(bytes_per_step) * args.steps)
+    return {"value": round(all_bytes / total / 1e9, 3), "unit": "GB/s",
+            "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
+            "ms_per_step": round(total / args.steps * 1e3, 5),
+            "gpu_launches_per_step": 2,
+            "path": "pinned H2D of q/new K,V rows/tables/lengths -> inferlab_cuda_kv_append -> "
+                    "inferlab_cuda_paged_decode -> D2H of the output, host wall clock"}
+
+
+def host_threads() -> int:
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
+def cpu_baseline_decode(batch, bytes_per_step, seconds: float) -> dict:
+    """The reference CPU kernel on the same pool contents, all host threads."""
+    from inferlab_b200 import workloads as wl
+    from oracle import oracle
+
+    k_host, v_host = wl.host_arenas(batch.pool)
+    q = wl.round_queries(batch.queries, batch.pool.dtype)
+    threads = host_threads()
+    sample = len(batch.contexts)
+    steps = 0
+    t0 = time.perf_counter()
+    while True:
+        oracle.reference_paged_decode_timed(k_host, v_host, batch.pool.dtype, batch.tables_host,
+                                            batch.contexts, q, batch.q_heads, threads)
+        steps += 1
+        elapsed = time.perf_counter() - t0
+        if elapsed >= seconds:
+            break
+    kind = "reference" if oracle.ref_lib() is not None else "port"
+    return {"value": round(bytes_per_step * steps / elapsed / 1e9, 4), "unit": "GB/s",
+            "cores": threads, "kind": kind,
+            "sample": f"{steps} full steps ({sample} sequences each) in {elapsed:.1f} s: page gather "
+                      "+ inferlab_attention_forward (OnlineTiled, tile 16) per q-head, "
+                      "oracle/_ref/libref.so built from kernels/attention_cpu.cpp"}
+
+
+def run_prefill(args, dist, world, rank, device, peaks, peak_kind):
+    import torch
+
+    from inferlab_b200 import workloads as wl
+
+    batch = wl.prefill_f16(device=device, seed=2028 + rank)
+    pool = batch.pool
+    stream = torch.cuda.current_stream(device)
+    flops = batch.prefill_flops()
+    out = torch.empty((batch.prefill_queries.shape[0], batch.q_heads, batch.head_dim),
+                      dtype=torch.float32, device=f"cuda:{device}")
+    flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=f"cuda:{device}")
+
+    def step():
+        pool.prefill(batch.prefill_queries, batch.prefill_tables, batch.starts_dev,
+                     batch.counts_dev, batch.offsets_dev, int(batch.counts.max()), out=out)
+
+    for i in range(args.warmup):
+        flush.fill_(float(i))
+        step()
+    pool.synchronize()
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    barrier(dist)
+    torch.cuda.synchronize(device)
+    with ClockSampler(device) as clocks:
+        for i in range(args.steps):
+            flush.fill_(float(i))
+            starts[i].record(stream)
+            step()
+            ends[i].record(stream)
+        torch.cuda.synchronize(device)
+        barrier(dist)
+    pool.synchronize()
+    kernel_ms = sum(s.elapsed_time(e) for s, e in zip(starts, ends))
+    total_ms = max_over_ranks(dist, kernel_ms)
+    all_flops = sum_over_ranks(dist, float(flops) * args.steps)
+    value = all_flops / (total_ms * 1e-3) / 1e12
+    achieved = flops / (kernel_ms / args.steps * 1e-3) / 1e12
+    peak = float(peaks["bf16_tflops"])
+    line = {
+        "metric": "prefill attn TFLOP/s", "value": round(value, 3), "unit": "TFLOP/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(total_ms / args.steps, 5), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f16",
+        "data": "synthetic (seeded N(0, 0.5^2))",
+        "config": {"workload": "causal prefill f16: 8 x 1024 tokens, 16 heads x 128, paged "
+                               "block 16", "flops_per_step": int(flops),
+                   "l2": "flushed between steps"},
+        "roofline": {"bound": "tensor", "achieved": round(achieved, 2), "peak": peak,
+                     "unit": "TFLOP/s", "frac": round(achieved / peak, 4),
+                     "peak_kind": f"{peak_kind} bf16_tflops (dense f16 = bf16 rate)",
+                     "traffic": read_traffic("paged_prefill_prefill_f16")},
+        "gpu_launches": args.steps, "clocks": clocks.summary(),
+    }
+    pool.close()
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if dist is not None:
+        dist.destroy_process_group()
+
+
+# ---------------------------------------------------------------------------
+# reference arm
+# ---------------------------------------------------------------------------
+def run_reference(args):
+    world, rank, _ = dist_env()
+    if rank != 0:
+        return
+    from oracle import oracle
+
+    if oracle.ref_lib() is None:
+        print(json.dumps({"impl": "reference",
+                          "unavailable": "oracle/_ref/libref.so was not built (reference sources "
+                                         "absent when the tree was prepared)"}), flush=True)
+        return
+    if args.workload != "decode_fp32":
+        print(json.dumps({"impl": "reference",
+                          "unavailable": f"reference arm implemented for decode_fp32 only"}),
+              flush=True)
+        return
+    # Host-side copy of the same workload shape (seeded numpy; no GPU on this path).
+    rng = np.random.Generator(np.random.PCG64(2026))
+    num_seqs, heads, head_dim, blocks = 64, 8, 64, 8192
+    contexts = rng.integers(64, 2048, size=num_seqs, endpoint=True)
+    need = (contexts + 15) // 16
+    perm = rng.permutation(blocks).astype(np.int32)
+    tables = np.zeros((num_seqs, 128), np.int32)
+    used = 0
+    for i, n in enumerate(need):
+        tables[i, :n] = perm[used:used + n]
+        used += n
+    k_arena = rng.standard_normal((blocks, heads, 16, head_dim), dtype=np.float32)
+    v_arena = rng.standard_normal((blocks, heads, 16, head_dim), dtype=np.float32)
+    q = rng.standard_normal((num_seqs, heads, head_dim), dtype=np.float32)
+    ctx = contexts.astype(np.int64)
+    bytes_per_step = (int(ctx.sum()) * heads * head_dim * 2 * 4 + 2 * num_seqs * heads * head_dim * 4
+                      + int(need.sum()) * 4 + num_seqs * 4)
+    threads = host_threads()
+    for _ in range(args.warmup):
+        oracle.reference_paged_decode_timed(k_arena, v_arena, 0, tables, contexts, q, heads,
+                                            threads)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        oracle.reference_paged_decode_timed(k_arena, v_arena, 0, tables, contexts, q, heads,
+                                            threads)
+    elapsed = time.perf_counter() - t0
+    value = bytes_per_step * args.steps / elapsed / 1e9
+    line = {
+        "impl": "reference", "metric": "decode attn KV-bytes GB/s", "value": round(value, 4),
+        "unit": "GB/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(elapsed / args.steps * 1e3, 4), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded N(0,1))",
+        "config": {"workload": "paged decode fp32: 64 seqs x ctx U[64,2048], 8 heads x 64 (MHA), "
+                               "block 16, 8192-block pool, random permutation tables",
+                   "num_seqs": num_seqs, "q_heads": heads, "kv_heads": heads,
+                   "head_dim": head_dim, "block_tokens": 16, "pool_blocks": blocks},
+        "cpu_baseline": {"value": round(value, 4), "unit": "GB/s", "cores": threads,
+                         "kind": "reference",
+                         "sample": "each step = the whole 64-sequence batch: page gather + "
+                                   "inferlab_attention_forward (OnlineTiled, tile 16) per q-head "
+                                   "from oracle/_ref/libref.so"},
+        "e2e": {"value": round(value, 4), "unit": "GB/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    parser = argparse.ArgumentParser()
+    parser.add_argument("--gpus", type=int, default=1)
+    parser.add_argument("--steps", type=int, default=20)
+    parser.add_argument("--warmup", type=int, default=5)
+    parser.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    parser.add_argument("--workload", default="decode_fp32",
+                        choices=["decode_fp32", "longctx_bf16", "prefill_f16"])
+    parser.add_argument("--cpu-seconds", type=float, default=10.0)
+    parser.add_argument("--no-cpu-baseline", action="store_true")
+    args = parser.parse_args()
+    args.warmup = max(args.warmup, 3)  # at least three untimed warm-up steps
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,268 @@
+/*
+ * inferlab_attention.h - C ABI of the B200 (sm_100a) attention library.
+ *
+ * Two groups of entry points:
+ *
+ *  1. The reference worker's attention entry, same signature and semantics:
+ *     inferlab_attention_forward() replaces the CPU implementation declared at
+ *     worker/cpp/inferlab_runtime.h:216-231 (implemented at
+ *     worker/cpp/inferlab_runtime.cpp:2561-2619 on top of
+ *     kernels/attention_cpu.cpp:419-502). Host buffers in, host buffer out;
+ *     the copies to and from HBM happen inside the call.
+ *
+ *  2. A device-resident paged KV pool and the kernels that read it through
+ *     block tables. They replace PagedKvPool's page storage, append and
+ *     materialize (worker/cpp/inferlab_runtime.cpp:649-1026) and the per-step
+ *     gather + attention_forward call of the paged decode branch
+ *     (worker/cpp/inferlab_runtime.cpp:2373-2393). Block-table semantics are
+ *     the reference's: logical block = position / block_tokens,
+ *     slot = position % block_tokens, physical block = table[logical block].
+ *     All pointers marked "device" are HBM pointers on the pool's device; all
+ *     calls are asynchronous on the given stream (NULL = the legacy default
+ *     stream) and take a cudaStream_t passed as void*.
+ *
+ * Error convention (both groups), as worker/cpp/inferlab_runtime.cpp:2013-2030:
+ * functions return 0 on success and -1 on failure, writing a NUL-terminated
+ * message truncated to error_capacity into `error` (which is cleared on entry).
+ * Host-side argument errors are reported by the call itself. Errors found by a
+ * kernel (a non-finite row, a block id outside the pool, an invalid
+ * normaliser) are recorded in the pool's device error word and reported by the
+ * next inferlab_cuda_pool_synchronize() on that pool.
+ */
+#ifndef INFERLAB_ATTENTION_H
+#define INFERLAB_ATTENTION_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* worker/cpp/inferlab_runtime.h:67-72 (field meaning from
+ * kernels/attention_cpu.h:8-24): algorithm 0 Materialized / 1 OnlineTiled,
+ * precision 0 Fp32 / 1 Fp16 / 2 Bf16 storage rounding, tile_tokens 1..4096,
+ * causal 0/1. */
+typedef struct InferlabAttentionConfig {
+    uint32_t algorithm;
+    uint32_t precision;
+    uint32_t tile_tokens;
+    uint32_t causal;
+} InferlabAttentionConfig;
+
+/* worker/cpp/inferlab_runtime.h:74-83; analytic counters computed exactly as
+ * kernels/attention_cpu.cpp:140-213 (they model the reference CPU algorithm;
+ * the CUDA kernels' own traffic is measured, not modelled). */
+typedef struct InferlabAttentionStats {
+    uint64_t score_elements;
+    uint64_t masked_score_elements;
+    uint64_t score_buffer_bytes;
+    uint64_t working_set_bytes;
+    uint64_t modeled_external_read_bytes;
+    uint64_t modeled_external_write_bytes;
+    uint64_t modeled_external_total_bytes;
+    uint64_t key_tiles;
+} InferlabAttentionStats;
+
+/*
+ * Replaces inferlab_attention_forward, worker/cpp/inferlab_runtime.h:216-231.
+ * queries [query_tokens][heads][head_dimension], keys/values
+ * [key_value_tokens][heads][head_dimension], output likewise for queries; all
+ * fp32 host memory. Validation order and messages follow
+ * worker/cpp/inferlab_runtime.cpp:2578-2593 and kernels/attention_cpu.cpp:432-447.
+ * Runs on the calling thread's current CUDA device. Both algorithms run the
+ * same fused online-softmax kernel in fp32 (storage rounding applied on load);
+ * the output matches either CPU algorithm within 1e-5 relative / 1e-6 absolute.
+ * head_dimension is limited to 4096 on the device.
+ */
+int inferlab_attention_forward(const float* queries, const float* keys, const float* values,
+                               size_t query_tokens, size_t key_value_tokens, size_t heads,
+                               size_t head_dimension, size_t query_start_position,
+                               const InferlabAttentionConfig* config, float* output,
+                               size_t output_capacity, InferlabAttentionStats* stats,
+                               char* error, size_t error_capacity);
+
+/* ------------------------------------------------------------------------ */
+/* Device-resident paged KV pool                                             */
+/* ------------------------------------------------------------------------ */
+
+/* Element type of a pool (same numbering as the attention precision). */
+#define INFERLAB_KV_FP32 0u
+#define INFERLAB_KV_F16 1u
+#define INFERLAB_KV_BF16 2u
+
+typedef struct InferlabCudaKvPool InferlabCudaKvPool;
+
+/* Geometry and device addresses of a pool. Each arena is
+ * [num_blocks][kv_heads][block_tokens][head_dim] elements of `dtype`: one
+ * block of one kv-head is a contiguous block_tokens x head_dim tile. */
+typedef struct InferlabCudaPoolInfo {
+    int32_t device;
+    uint32_t dtype;
+    uint32_t block_tokens;
+    uint32_t kv_heads;
+    uint32_t head_dim;
+    uint32_t element_bytes;
+    uint64_t num_blocks;
+    uint64_t block_bytes;  /* bytes of one block in one arena, all kv-heads */
+    uint64_t arena_bytes;  /* bytes of one arena */
+    void* key_arena;       /* device */
+    void* value_arena;     /* device */
+} InferlabCudaPoolInfo;
+
+/*
+ * Allocates a pool of num_blocks blocks in HBM on `device` (the device pool
+ * behind PagedKvPool's page storage, worker/cpp/inferlab_runtime.cpp:657-678,
+ * configured like inferlab_model_configure_paged_cache, :2157-2189; the
+ * reference's 65,536-page cap is lifted because HBM holds ~180 GB). The arenas
+ * are zero-filled. Block ids are int32, so num_blocks < 2^31.
+ */
+int inferlab_cuda_pool_create(int32_t device, uint32_t dtype, uint64_t num_blocks,
+                              uint32_t block_tokens, uint32_t kv_heads, uint32_t head_dim,
+                              InferlabCudaKvPool** pool, char* error, size_t error_capacity);
+
+/* Frees the arenas (after synchronising the device). NULL is a no-op. */
+void inferlab_cuda_pool_destroy(InferlabCudaKvPool* pool);
+
+int inferlab_cuda_pool_info(const InferlabCudaKvPool* pool, InferlabCudaPoolInfo* info,
+                            char* error, size_t error_capacity);
+
+/*
+ * Waits for `stream` for at most timeout_ms milliseconds (0 = 10 s), then
+ * reads and clears the pool's device error word. Returns -1 with the first
+ * recorded error ("paged KV block table contains an invalid page",
+ * "attention input must be finite", "online attention normalizer is
+ * invalid", "paged KV context length is invalid", ...) or with
+ * "CUDA stream wait timed out" when the stream is still busy.
+ */
+int inferlab_cuda_pool_synchronize(InferlabCudaKvPool* pool, void* stream, uint32_t timeout_ms,
+                                   char* error, size_t error_capacity);
+
+/*
+ * Writes `rows` token rows into the pool (the data movement of
+ * PagedKvPool::append, worker/cpp/inferlab_runtime.cpp:713-767, without its
+ * host-side allocation policy). Row r is key_rows[r] / value_rows[r], each
+ * [kv_heads][head_dim] of `row_dtype` (INFERLAB_KV_FP32, rounded to the pool
+ * type like round_attention_value, kernels/attention_cpu.cpp:405-417; or the
+ * pool's own type, copied bit for bit), and goes to position positions[r] of
+ * sequence row_sequences[r]: block block_tables[seq * max_blocks_per_seq +
+ * pos / block_tokens], slot pos % block_tokens. Non-finite values are
+ * rejected ("attention input must be finite"); the row is not written.
+ * All arrays are device memory.
+ */
+int inferlab_cuda_kv_append(InferlabCudaKvPool* pool, const void* key_rows, const void* value_rows,
+                            uint32_t row_dtype, const int32_t* row_sequences,
+                            const int32_t* positions, uint64_t rows, const int32_t* block_tables,
+                            uint32_t max_blocks_per_seq, void* stream, char* error,
+                            size_t error_capacity);
+
+/*
+ * Copies the first `tokens` positions of one sequence into contiguous
+ * [tokens][kv_heads][head_dim] arrays of the pool's type, bit for bit: the
+ * device form of PagedKvPool::materialize (worker/cpp/inferlab_runtime.cpp:
+ * 769-803). block_table holds ceil(tokens / block_tokens) device int32 ids.
+ */
+int inferlab_cuda_kv_gather(InferlabCudaKvPool* pool, const int32_t* block_table, uint64_t tokens,
+                            void* keys_out, void* values_out, void* stream, char* error,
+                            size_t error_capacity);
+
+/*
+ * Bytes of device workspace inferlab_cuda_paged_decode needs for this batch
+ * shape. max_context_len bounds every context_lens[i].
+ */
+size_t inferlab_cuda_paged_decode_workspace_size(const InferlabCudaKvPool* pool, uint32_t num_seqs,
+                                                 uint32_t q_heads, uint32_t max_context_len);
+
+/*
+ * Zeroes the counters at the front of a decode workspace. Needed once per
+ * workspace before its first use; the decode kernel leaves them at zero.
+ */
+int inferlab_cuda_paged_decode_workspace_init(void* workspace, size_t workspace_bytes,
+                                              void* stream, char* error, size_t error_capacity);
+
+/*
+ * One decode step for a batch: sequence i has one query token at position
+ * context_lens[i] - 1 attending to positions [0, context_lens[i]) of its
+ * block table row (the call shape of worker/cpp/inferlab_runtime.cpp:
+ * 1458-1470, attention_forward(q, K, V, 1, T, H, d, T - 1)).
+ * queries: device fp32 [num_seqs][q_heads][head_dim], rounded to the pool's
+ * type on load (the reference's Fp16/Bf16 storage modes round queries too).
+ * q-head h reads kv-head h / (q_heads / kv_heads) (grouped-query attention;
+ * q_heads must be a multiple of kv_heads). block_tables: device int32
+ * [num_seqs][max_blocks_per_seq]. context_lens: device int32 [num_seqs],
+ * each in [1, max_context_len] and <= max_blocks_per_seq * block_tokens.
+ * out: device fp32 [num_seqs][q_heads][head_dim]. Long contexts are split
+ * across CTAs and merged by log-sum-exp inside the same launch; workspace
+ * (inferlab_cuda_paged_decode_workspace_size bytes, initialised once with
+ * inferlab_cuda_paged_decode_workspace_init) holds the split partials.
+ */
+int inferlab_cuda_paged_decode(InferlabCudaKvPool* pool, const float* queries,
+                               const int32_t* block_tables, uint32_t max_blocks_per_seq,
+                               const int32_t* context_lens, uint32_t num_seqs, uint32_t q_heads,
+                               uint32_t max_context_len, float* out, void* workspace,
+                               size_t workspace_bytes, void* stream, char* error,
+                               size_t error_capacity);
+
+/*
+ * Decode partials for a context that is split across devices: like
+ * inferlab_cuda_paged_decode, but instead of the normalised output it writes,
+ * per (sequence, q-head) row r = seq * q_heads + h,
+ *   part_m[r] = max score (natural-log units, scores already scaled by
+ *               1/sqrt(head_dim)),
+ *   part_l[r] = sum exp(score - part_m[r]),
+ *   part_o[r][d] = sum exp(score - part_m[r]) * v[d]   (unnormalised),
+ * over every position the block table row covers (all of them are visible to
+ * the query: it sits after the whole local range). Rows with no keys get
+ * m = -inf, l = 0, o = 0. The parts are merged with inferlab_cuda_lse_combine.
+ */
+int inferlab_cuda_paged_decode_partials(InferlabCudaKvPool* pool, const float* queries,
+                                        const int32_t* block_tables, uint32_t max_blocks_per_seq,
+                                        const int32_t* context_lens, uint32_t num_seqs,
+                                        uint32_t q_heads, uint32_t max_context_len, float* part_m,
+                                        float* part_l, float* part_o, void* workspace,
+                                        size_t workspace_bytes, void* stream, char* error,
+                                        size_t error_capacity);
+
+/*
+ * Log-sum-exp merge of `parts` partial results in part order (deterministic):
+ * part_m, part_l [parts][rows], part_o [parts][rows][head_dim], all device fp32;
+ * out [rows][head_dim] = sum_i o_i e^(m_i - M) / sum_i l_i e^(m_i - M),
+ * M = max over parts with l_i > 0.
+ */
+int inferlab_cuda_lse_combine(const float* part_m, const float* part_l, const float* part_o,
+                              uint32_t parts, uint64_t rows, uint32_t head_dim, float* out,
+                              void* stream, char* error, size_t error_capacity);
+
+/*
+ * Causal prefill / chunked prefill over the paged pool. Segment s has
+ * query_counts[s] query tokens at positions [query_starts[s],
+ * query_starts[s] + query_counts[s]) of its sequence, whose keys and values
+ * for positions [0, query_starts[s] + query_counts[s]) are already in the
+ * pool under block table row s; query i attends to positions
+ * [0, query_starts[s] + i] (legal_sources, kernels/attention_cpu.cpp:113-123).
+ * queries: device [total_queries][q_heads][head_dim] of query_dtype
+ * (INFERLAB_KV_FP32 is rounded to the pool type; otherwise it must equal the
+ * pool type); segment s uses rows [query_offsets[s], query_offsets[s] +
+ * query_counts[s]), and the segments tile [0, total_queries) in order.
+ * query_starts, query_counts, query_offsets: device int32 [num_segments].
+ * out: device fp32 [total_queries][q_heads][head_dim].
+ * f16/bf16 pools with head_dim 128 and block_tokens 16 run on the tcgen05
+ * tensor cores (fp32 accumulation in TMEM); other pools run a fp32 CUDA-core
+ * kernel. max_query_count bounds every query_counts[s].
+ */
+int inferlab_cuda_paged_prefill(InferlabCudaKvPool* pool, const void* queries, uint32_t query_dtype,
+                                const int32_t* block_tables, uint32_t max_blocks_per_seq,
+                                const int32_t* query_starts, const int32_t* query_counts,
+                                const int32_t* query_offsets, uint32_t num_segments,
+                                uint32_t q_heads, uint32_t max_query_count,
+                                uint64_t total_queries, float* out, void* stream, char* error,
+                                size_t error_capacity);
+
+/* Library version string, e.g. "inferlab-b200 0.1 sm_100a". */
+const char* inferlab_cuda_version(void);
+
+#ifdef __cplusplus
+}  /* extern "C" */
+#endif
+
+#endif /* INFERLAB_ATTENTION_H */

@@ -1,0 +1,257 @@
+// common.cuh - shared pieces of the sm_100a attention library: host error
+// plumbing (the reference's status + message convention), storage rounding,
+// the device error word, and inline-PTX wrappers for mbarriers and bulk
+// asynchronous copies (TMA engine, no multicast).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cuda_fp16.h>
+#include <cuda_bf16.h>
+
+#include <cstddef>
+#include <cstdint>
+#include <cstring>
+#include <stdexcept>
+#include <string>
+
+namespace ilb {
+
+// ---------------------------------------------------------------------------
+// Host error convention: worker/cpp/inferlab_runtime.cpp:1965-1978 (message
+// truncated to capacity, cleared on entry) and :2013-2030 (exceptions become
+// status -1, nothing crosses the C ABI).
+// ---------------------------------------------------------------------------
+inline void write_error(char* error, std::size_t capacity, const std::string& message) {
+    if (error == nullptr || capacity == 0) return;
+    const std::size_t count = message.size() < capacity - 1 ? message.size() : capacity - 1;
+    std::memcpy(error, message.data(), count);
+    error[count] = '\0';
+}
+
+inline void clear_error(char* error, std::size_t capacity) {
+    if (error != nullptr && capacity > 0) error[0] = '\0';
+}
+
+template <typename F>
+int protect(char* error, std::size_t capacity, F&& body) noexcept {
+    try {
+        clear_error(error, capacity);
+        body();
+        return 0;
+    } catch (const std::exception& caught) {
+        write_error(error, capacity, caught.what());
+        return -1;
+    } catch (...) {
+        write_error(error, capacity, "unknown CUDA runtime failure");
+        return -1;
+    }
+}
+
+inline void cuda_check(cudaError_t status, const char* what) {
+    if (status != cudaSuccess) {
+        throw std::runtime_error(std::string(what) + ": " + cudaGetErrorString(status));
+    }
+}
+
+// Restores the calling thread's current device on scope exit.
+class DeviceGuard {
+public:
+    explicit DeviceGuard(int device) {
+        cuda_check(cudaGetDevice(&previous_), "cudaGetDevice");
+        if (device != previous_) cuda_check(cudaSetDevice(device), "cudaSetDevice");
+    }
+    ~DeviceGuard() {
+        int now = -1;
+        if (cudaGetDevice(&now) == cudaSuccess && now != previous_) cudaSetDevice(previous_);
+    }
+    DeviceGuard(const DeviceGuard&) = delete;
+    DeviceGuard& operator=(const DeviceGuard&) = delete;
+
+private:
+    int previous_ = 0;
+};
+
+inline std::size_t checked_mul(std::size_t a, std::size_t b, const char* message) {
+    if (a != 0 && b > SIZE_MAX / a) throw std::runtime_error(message);
+    return a * b;
+}
+
+// Waits for all work queued on `stream` with a deadline; throws on timeout.
+void wait_stream(cudaStream_t stream, std::uint32_t timeout_ms);
+
+// ---------------------------------------------------------------------------
+// Device error word: kernels OR these bits in; the host maps them to the
+// reference's messages.
+// ---------------------------------------------------------------------------
+enum ErrorBits : std::uint32_t {
+    kErrNonFinite = 1u << 0,     // "attention input must be finite"
+    kErrBadBlock = 1u << 1,      // "paged KV block table contains an invalid page"
+    kErrNormalizer = 1u << 2,    // "online attention normalizer is invalid"
+    kErrContext = 1u << 3,       // "paged KV context length is invalid"
+    kErrSegment = 1u << 4,       // "paged prefill segment is invalid"
+    kErrWaitTimeout = 1u << 5,   // "device wait timed out"
+    kErrPosition = 1u << 6,      // "paged KV append position is outside the block table"
+};
+
+std::string describe_error_bits(std::uint32_t bits);
+
+__device__ __forceinline__ void flag_error(std::uint32_t* word, std::uint32_t bit) {
+    if (word != nullptr) atomicOr(word, bit);
+}
+
+// ---------------------------------------------------------------------------
+// Storage precision (kernels/attention_cpu.cpp:405-417): fp32 -> fp16/bf16
+// with round to nearest even and back. The CUDA conversions are IEEE RNE, the
+// same rounding the reference implements bit by bit; tests compare the two
+// over random bit patterns.
+// ---------------------------------------------------------------------------
+enum StorageType : std::uint32_t { kFp32 = 0, kF16 = 1, kBf16 = 2 };
+
+__device__ __forceinline__ float round_storage(float x, std::uint32_t precision) {
+    if (precision == kF16) return __half2float(__float2half_rn(x));
+    if (precision == kBf16) return __bfloat162float(__float2bfloat16_rn(x));
+    return x;
+}
+
+template <typename T>
+struct Storage;
+template <>
+struct Storage<float> {
+    static constexpr std::uint32_t kType = kFp32;
+    __device__ __forceinline__ static float to_float(float x) { return x; }
+    __device__ __forceinline__ static float from_float(float x) { return x; }
+};
+template <>
+struct Storage<__half> {
+    static constexpr std::uint32_t kType = kF16;
+    __device__ __forceinline__ static float to_float(__half x) { return __half2float(x); }
+    __device__ __forceinline__ static __half from_float(float x) { return __float2half_rn(x); }
+};
+template <>
+struct Storage<__nv_bfloat16> {
+    static constexpr std::uint32_t kType = kBf16;
+    __device__ __forceinline__ static float to_float(__nv_bfloat16 x) { return __bfloat162float(x); }
+    __device__ __forceinline__ static __nv_bfloat16 from_float(float x) {
+        return __float2bfloat16_rn(x);
+    }
+};
+
+// Widen a 16-byte chunk of storage elements to floats.
+__device__ __forceinline__ void widen16(const uint4& raw, float* out, float) {
+    out[0] = __uint_as_float(raw.x);
+    out[1] = __uint_as_float(raw.y);
+    out[2] = __uint_as_float(raw.z);
+    out[3] = __uint_as_float(raw.w);
+}
+__device__ __forceinline__ void widen16(const uint4& raw, float* out, __half) {
+    const __half2* h = reinterpret_cast<const __half2*>(&raw);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const float2 f = __half22float2(h[i]);
+        out[2 * i] = f.x;
+        out[2 * i + 1] = f.y;
+    }
+}
+__device__ __forceinline__ void widen16(const uint4& raw, float* out, __nv_bfloat16) {
+    // bf16 -> fp32 is a 16-bit shift of the bit pattern.
+    const std::uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        out[2 * i] = __uint_as_float(w[i] << 16);
+        out[2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u);
+    }
+}
+
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kLn2 = 0.6931471805599453f;
+
+// ---------------------------------------------------------------------------
+// mbarrier + bulk async copy (sm_90+ PTX; used here on sm_100a). Copies are
+// issued by one thread; completion is tracked by the mbarrier's transaction
+// count. No cluster multicast anywhere in this library.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ std::uint32_t smem_u32(const void* p) {
+    return static_cast<std::uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(std::uint64_t* bar, std::uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count)
+                 : "memory");
+}
+
+__device__ __forceinline__ void fence_barrier_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void fence_proxy_async_shared() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(std::uint64_t* bar, std::uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
+                 "r"(bytes)
+                 : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(std::uint64_t* bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(std::uint64_t* bar, std::uint32_t parity) {
+    std::uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(done)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return done != 0;
+}
+
+__device__ __forceinline__ std::uint64_t global_timer_ns() {
+    std::uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+// Bounded wait on an mbarrier phase. Returns false (and records
+// kErrWaitTimeout) when the phase has not completed within ~timeout_ns.
+__device__ __forceinline__ bool mbar_wait_bounded(std::uint64_t* bar, std::uint32_t parity,
+                                                  std::uint32_t* error_word,
+                                                  std::uint64_t timeout_ns = 2000000000ull) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const std::uint64_t start = global_timer_ns();
+    for (std::uint32_t spins = 1;; ++spins) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if ((spins & 255u) == 0 && global_timer_ns() - start > timeout_ns) {
+            flag_error(error_word, kErrWaitTimeout);
+            return false;
+        }
+    }
+}
+
+// Bulk copy of `bytes` (multiple of 16, both addresses 16-byte aligned) from
+// global to this CTA's shared memory, completing on `bar`.
+__device__ __forceinline__ void bulk_copy_g2s(void* dst, const void* src, std::uint32_t bytes,
+                                              std::uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::
+            "r"(smem_u32(dst)),
+        "l"(src), "r"(bytes), "r"(smem_u32(bar))
+        : "memory");
+}
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, off));
+    return v;
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+    return v;
+}
+
+}  // namespace ilb

@@ -1,0 +1,762 @@
+// paged_decode.cu - memory-bound paged decode attention for sm_100a.
+//
+// The decode branch of the reference (worker/cpp/inferlab_runtime.cpp:
+// 2373-2393) gathers every page of a sequence into contiguous fp32
+// (PagedKvPool::materialize, :769-803) and then runs the scalar
+// attention_forward(q, K, V, 1, T, H, d, T - 1) (:1458-1470,
+// kernels/attention_cpu.cpp:306-401). Here one launch covers the whole batch
+// and reads the pool in place:
+//
+//  * grid: one CTA per (sequence, kv-head, split); a split is up to
+//    blocks_per_split consecutive 16-token blocks of the context.
+//  * each warp streams its own blocks (block w, w + W, ...) through a
+//    STAGES-deep ring of shared-memory tiles. Lane 0 issues one bulk async
+//    copy (cp.async.bulk, the TMA engine, no multicast) per tile: the K and V
+//    tiles of one block for one kv-head are each a contiguous
+//    16 x head_dim run in the arena, completion tracked by an mbarrier.
+//  * lanes split as (token slot, 16-byte chunk group): kG lanes share one
+//    token row, each holding kDpl dims of every q-head of the GQA group in
+//    registers; dot products reduce with kG-wide xor shuffles; every token
+//    slot keeps its own online-softmax state (m, l, acc) in the log2 domain.
+//  * at the end the slot states merge by shuffles, the warps by shared
+//    memory, and - when the context was split - the CTAs by a fused
+//    log-sum-exp combine: every CTA writes (m, l, acc) to the workspace, and
+//    the last CTA of its (sequence, kv-head) to arrive merges all splits and
+//    writes the output.
+//
+// K/V bytes are read from HBM exactly once per (sequence, kv-head).
+#include "common.cuh"
+#include "generic_attention.cuh"
+#include "pool.cuh"
+
+#include "../../include/inferlab_attention.h"
+
+#include <algorithm>
+#include <cmath>
+#include <cstdlib>
+
+namespace ilb {
+namespace {
+
+constexpr int kDecodeBlockTokens = 16;
+constexpr int kDecodeWarps = 4;
+constexpr int kDecodeStages = 2;
+constexpr int kMaxBlocksPerSplit = 256;
+
+template <typename KvT, int D, int GROUP>
+struct DecodeShape {
+    static constexpr int kElem = sizeof(KvT);
+    static constexpr int kEpc = 16 / kElem;              // elements per 16-byte chunk
+    static constexpr int kChunks = D * kElem / 16;       // chunks per token row
+    static constexpr int kChA = kChunks / 8 > 0 ? kChunks / 8 : 1;
+    static constexpr int kChB = 64 / (GROUP * kEpc) > 0 ? 64 / (GROUP * kEpc) : 1;
+    static constexpr int kCh = kChA < kChB ? kChA : kChB;  // chunks per lane
+    static constexpr int kG = kChunks / kCh;             // lanes per token row
+    static constexpr int kTS = 32 / kG;                  // token slots per warp
+    static constexpr int kR = kDecodeBlockTokens / kTS;  // tokens per slot per block
+    static constexpr int kDpl = kCh * kEpc;              // dims per lane
+    static constexpr int kTileBytes = kDecodeBlockTokens * D * kElem;
+    static_assert(kChunks * 16 == D * kElem, "head_dim must fill 16-byte chunks");
+    static_assert(kG >= 1 && kG <= 32 && 32 % kG == 0, "lane split");
+    static_assert(kDecodeBlockTokens % kTS == 0, "token slots");
+};
+
+struct DecodeParams {
+    const unsigned char* key_arena;
+    const unsigned char* value_arena;
+    std::uint64_t num_blocks;
+    std::uint32_t kv_heads;
+    const float* queries;
+    std::uint32_t q_heads;
+    const std::int32_t* tables;
+    std::uint32_t max_blocks;
+    const std::int32_t* context_lens;
+    std::uint32_t max_context;
+    std::uint32_t blocks_per_split;
+    std::uint32_t max_splits;
+    float scale_log2;
+    int emit_partials;  // 0: normalised out; 1: (m, l, o) rows
+    float* out;
+    float* part_m;
+    float* part_l;
+    float* part_o;
+    float* ws_o;             // [seq][q_head][split][D]
+    float* ws_ml;            // [seq][q_head][split][2]
+    std::uint32_t* ws_count; // [seq][kv_head]
+    std::uint32_t* error_word;
+};
+
+// Shared-memory layout of one CTA.
+template <typename KvT, int D, int GROUP>
+struct DecodeSmem {
+    using S = DecodeShape<KvT, D, GROUP>;
+    static constexpr std::size_t kTiles = 0;
+    static constexpr std::size_t kTilesBytes =
+        static_cast<std::size_t>(kDecodeWarps) * kDecodeStages * 2 * S::kTileBytes;
+    static constexpr std::size_t kBars = kTilesBytes;
+    static constexpr std::size_t kIds = kBars + kDecodeWarps * kDecodeStages * 8;
+    static constexpr std::size_t kRedAcc = kIds + kMaxBlocksPerSplit * 4;
+    static constexpr std::size_t kRedMl = kRedAcc + static_cast<std::size_t>(kDecodeWarps) * GROUP * D * 4;
+    static constexpr std::size_t kFlag = kRedMl + kDecodeWarps * GROUP * 2 * 4;
+    static constexpr std::size_t kBytes = kFlag + 16;
+};
+
+__device__ __forceinline__ float safe_max(float m) { return m == -INFINITY ? 0.0f : m; }
+
+template <typename KvT, int D, int GROUP>
+__global__ void __launch_bounds__(kDecodeWarps * 32)
+    paged_decode_kernel(const DecodeParams p) {
+    using S = DecodeShape<KvT, D, GROUP>;
+    using L = DecodeSmem<KvT, D, GROUP>;
+    extern __shared__ __align__(128) unsigned char smem[];
+    auto* bars = reinterpret_cast<std::uint64_t*>(smem + L::kBars);
+    auto* ids = reinterpret_cast<std::int32_t*>(smem + L::kIds);
+    auto* red_acc = reinterpret_cast<float*>(smem + L::kRedAcc);
+    auto* red_ml = reinterpret_cast<float*>(smem + L::kRedMl);
+    auto* flag = reinterpret_cast<int*>(smem + L::kFlag);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const std::uint32_t split = blockIdx.x % p.max_splits;
+    const std::uint32_t pair = blockIdx.x / p.max_splits;
+    const std::uint32_t kv_head = pair % p.kv_heads;
+    const std::uint32_t seq = pair / p.kv_heads;
+    const std::size_t row0 = static_cast<std::size_t>(seq) * p.q_heads + kv_head * GROUP;
+
+    const int ctx = p.context_lens[seq];
+    const int max_ctx = static_cast<int>(min(p.max_context, p.max_blocks * kDecodeBlockTokens));
+    if (ctx < 1 || ctx > max_ctx) {
+        if (split == 0) {
+            if (threadIdx.x == 0) flag_error(p.error_word, kErrContext);
+            for (int i = threadIdx.x; i < GROUP * D; i += blockDim.x) {
+                if (p.emit_partials) {
+                    p.part_o[row0 * D + i] = 0.0f;
+                    if (i % D == 0) {
+                        p.part_m[row0 + i / D] = -INFINITY;
+                        p.part_l[row0 + i / D] = 0.0f;
+                    }
+                } else {
+                    p.out[row0 * D + i] = 0.0f;
+                }
+            }
+        }
+        return;
+    }
+    const int nblk = (ctx + kDecodeBlockTokens - 1) / kDecodeBlockTokens;
+    const int bps = static_cast<int>(p.blocks_per_split);
+    const int nsplit = (nblk + bps - 1) / bps;
+    if (static_cast<int>(split) >= nsplit) return;
+    const int b0 = static_cast<int>(split) * bps;
+    const int nb = min(nblk - b0, bps);
+
+    for (int i = threadIdx.x; i < nb; i += blockDim.x) {
+        std::int32_t id = p.tables[static_cast<std::size_t>(seq) * p.max_blocks + b0 + i];
+        if (id < 0 || static_cast<std::uint64_t>(id) >= p.num_blocks) {
+            flag_error(p.error_word, kErrBadBlock);
+            id = 0;
+        }
+        ids[i] = id;
+    }
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kDecodeWarps * kDecodeStages; ++s) mbar_init(&bars[s], 1);
+        *flag = 0;
+        fence_barrier_init();
+    }
+    __syncthreads();
+
+    // Queries of the GQA group, rounded to the pool type (the reference rounds
+    // Q in its Fp16/Bf16 modes, kernels/attention_cpu.cpp:456-457).
+    const int ts = lane / S::kG;
+    const int cg = lane % S::kG;
+    float q[GROUP][S::kDpl];
+    bool q_bad = false;
+#pragma unroll
+    for (int h = 0; h < GROUP; ++h) {
+        const float* qrow = p.queries + (row0 + h) * D;
+#pragma unroll
+        for (int c = 0; c < S::kCh; ++c) {
+            const int base = (cg + S::kG * c) * S::kEpc;
+#pragma unroll
+            for (int e = 0; e < S::kEpc; e += 4) {
+                const float4 v = *reinterpret_cast<const float4*>(qrow + base + e);
+                const float raw[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+                for (int t = 0; t < 4; ++t) {
+                    q_bad |= !isfinite(raw[t]);
+                    q[h][c * S::kEpc + e + t] = round_storage(raw[t], Storage<KvT>::kType);
+                }
+            }
+        }
+    }
+    if (q_bad) flag_error(p.error_word, kErrNonFinite);
+
+    // This warp's blocks: local index warp, warp + W, ...
+    const int my_count = warp < nb ? (nb - warp + kDecodeWarps - 1) / kDecodeWarps : 0;
+    unsigned char* tiles = smem + static_cast<std::size_t>(warp) * kDecodeStages * 2 * S::kTileBytes;
+    std::uint64_t* my_bars = bars + warp * kDecodeStages;
+    const std::size_t head_offset = static_cast<std::size_t>(kv_head) * S::kTileBytes;
+    const std::size_t block_stride = static_cast<std::size_t>(p.kv_heads) * S::kTileBytes;
+    auto issue = [&](int j) {
+        const int stage = j % kDecodeStages;
+        const std::size_t src = static_cast<std::size_t>(ids[warp + j * kDecodeWarps]) * block_stride +
+                                head_offset;
+        unsigned char* dst = tiles + static_cast<std::size_t>(stage) * 2 * S::kTileBytes;
+        mbar_arrive_expect_tx(&my_bars[stage], 2 * S::kTileBytes);
+        bulk_copy_g2s(dst, p.key_arena + src, S::kTileBytes, &my_bars[stage]);
+        bulk_copy_g2s(dst + S::kTileBytes, p.value_arena + src, S::kTileBytes, &my_bars[stage]);
+    };
+    if (lane == 0) {
+        for (int j = 0; j < min(my_count, kDecodeStages); ++j) issue(j);
+    }
+
+    float m[GROUP];
+    float l[GROUP];
+    float acc[GROUP][S::kDpl];
+#pragma unroll
+    for (int h = 0; h < GROUP; ++h) {
+        m[h] = -INFINITY;
+        l[h] = 0.0f;
+#pragma unroll
+        for (int e = 0; e < S::kDpl; ++e) acc[h][e] = 0.0f;
+    }
+
+    int consumed = 0;
+    for (int j = 0; j < my_count; ++j) {
+        const int stage = j % kDecodeStages;
+        if (!mbar_wait_bounded(&my_bars[stage], (j / kDecodeStages) & 1, p.error_word)) {
+            *flag = 1;
+            break;
+        }
+        consumed = j + 1;
+        const unsigned char* ktile = tiles + static_cast<std::size_t>(stage) * 2 * S::kTileBytes;
+        const unsigned char* vtile = ktile + S::kTileBytes;
+        const int first_token = (b0 + warp + j * kDecodeWarps) * kDecodeBlockTokens;
+        const int valid = min(kDecodeBlockTokens, ctx - first_token);
+
+        float s[GROUP][S::kR];
+#pragma unroll
+        for (int r = 0; r < S::kR; ++r) {
+            const int trow = ts + S::kTS * r;
+            float part[GROUP];
+#pragma unroll
+            for (int h = 0; h < GROUP; ++h) part[h] = 0.0f;
+#pragma unroll
+            for (int c = 0; c < S::kCh; ++c) {
+                const uint4 raw = *reinterpret_cast<const uint4*>(
+                    ktile + (static_cast<std::size_t>(trow) * S::kChunks + cg + S::kG * c) * 16);
+                float kf[S::kEpc];
+                widen16(raw, kf, KvT{});
+#pragma unroll
+                for (int h = 0; h < GROUP; ++h) {
+#pragma unroll
+                    for (int e = 0; e < S::kEpc; ++e) part[h] = fmaf(q[h][c * S::kEpc + e], kf[e], part[h]);
+                }
+            }
+#pragma unroll
+            for (int h = 0; h < GROUP; ++h) s[h][r] = part[h];
+        }
+#pragma unroll
+        for (int off = 1; off < S::kG; off <<= 1) {
+#pragma unroll
+            for (int h = 0; h < GROUP; ++h) {
+#pragma unroll
+                for (int r = 0; r < S::kR; ++r) s[h][r] += __shfl_xor_sync(0xffffffffu, s[h][r], off);
+            }
+        }
+#pragma unroll
+        for (int h = 0; h < GROUP; ++h) {
+            float mx = -INFINITY;
+#pragma unroll
+            for (int r = 0; r < S::kR; ++r) {
+                s[h][r] = (ts + S::kTS * r) < valid ? s[h][r] * p.scale_log2 : -INFINITY;
+                mx = fmaxf(mx, s[h][r]);
+            }
+            const float m_new = fmaxf(m[h], mx);
+            const float base = safe_max(m_new);
+            const float alpha = exp2f(m[h] - base);
+            m[h] = m_new;
+            float sum = 0.0f;
+#pragma unroll
+            for (int r = 0; r < S::kR; ++r) {
+                s[h][r] = exp2f(s[h][r] - base);
+                sum += s[h][r];
+            }
+            l[h] = l[h] * alpha + sum;
+#pragma unroll
+            for (int e = 0; e < S::kDpl; ++e) acc[h][e] *= alpha;
+        }
+#pragma unroll
+        for (int r = 0; r < S::kR; ++r) {
+            const int trow = ts + S::kTS * r;
+            if (trow >= valid) continue;
+#pragma unroll
+            for (int c = 0; c < S::kCh; ++c) {
+                const uint4 raw = *reinterpret_cast<const uint4*>(
+                    vtile + (static_cast<std::size_t>(trow) * S::kChunks + cg + S::kG * c) * 16);
+                float vf[S::kEpc];
+                widen16(raw, vf, KvT{});
+#pragma unroll
+                for (int h = 0; h < GROUP; ++h) {
+#pragma unroll
+                    for (int e = 0; e < S::kEpc; ++e) {
+                        acc[h][c * S::kEpc + e] = fmaf(s[h][r], vf[e], acc[h][c * S::kEpc + e]);
+                    }
+                }
+            }
+        }
+        __syncwarp();
+        if (lane == 0 && j + kDecodeStages < my_count) issue(j + kDecodeStages);
+    }
+    if (*flag) {
+        // A wait gave up: drain this warp's copies still in flight (bounded)
+        // before the CTA's shared memory can be released.
+        for (int j = consumed; j < min(my_count, consumed + kDecodeStages); ++j) {
+            mbar_wait_bounded(&my_bars[j % kDecodeStages], (j / kDecodeStages) & 1, p.error_word);
+        }
+    }
+
+    // Merge the token-slot states inside the warp (butterfly over slot bits).
+#pragma unroll
+    for (int off = S::kG; off < 32; off <<= 1) {
+#pragma unroll
+        for (int h = 0; h < GROUP; ++h) {
+            const float mo = __shfl_xor_sync(0xffffffffu, m[h], off);
+            const float lo = __shfl_xor_sync(0xffffffffu, l[h], off);
+            const float mn = fmaxf(m[h], mo);
+            const float base = safe_max(mn);
+            const float a = exp2f(m[h] - base);
+            const float b = exp2f(mo - base);
+            l[h] = l[h] * a + lo * b;
+#pragma unroll
+            for (int e = 0; e < S::kDpl; ++e) {
+                const float other = __shfl_xor_sync(0xffffffffu, acc[h][e], off);
+                acc[h][e] = acc[h][e] * a + other * b;
+            }
+            m[h] = mn;
+        }
+    }
+    if (ts == 0) {
+#pragma unroll
+        for (int h = 0; h < GROUP; ++h) {
+            float* dst = red_acc + (static_cast<std::size_t>(warp) * GROUP + h) * D;
+#pragma unroll
+            for (int c = 0; c < S::kCh; ++c) {
+#pragma unroll
+                for (int e = 0; e < S::kEpc; ++e) {
+                    dst[(cg + S::kG * c) * S::kEpc + e] = acc[h][c * S::kEpc + e];
+                }
+            }
+            if (cg == 0) {
+                red_ml[(warp * GROUP + h) * 2] = m[h];
+                red_ml[(warp * GROUP + h) * 2 + 1] = l[h];
+            }
+        }
+    }
+    __syncthreads();
+    if (*flag) return;
+
+    // Merge the warps; write the output or this split's partial.
+    const bool single = nsplit == 1;
+    for (int i = threadIdx.x; i < GROUP * D; i += blockDim.x) {
+        const int h = i / D;
+        const int dim = i % D;
+        float mw = -INFINITY;
+#pragma unroll
+        for (int w = 0; w < kDecodeWarps; ++w) mw = fmaxf(mw, red_ml[(w * GROUP + h) * 2]);
+        const float base = safe_max(mw);
+        float lsum = 0.0f;
+        float a = 0.0f;
+#pragma unroll
+        for (int w = 0; w < kDecodeWarps; ++w) {
+            const float f = exp2f(red_ml[(w * GROUP + h) * 2] - base);
+            lsum += red_ml[(w * GROUP + h) * 2 + 1] * f;
+            a += red_acc[(static_cast<std::size_t>(w) * GROUP + h) * D + dim] * f;
+        }
+        const std::size_t row = row0 + h;
+        if (single) {
+            if (p.emit_partials) {
+                p.part_o[row * D + dim] = a;
+                if (dim == 0) {
+                    p.part_m[row] = mw * kLn2;
+                    p.part_l[row] = lsum;
+                }
+            } else {
+                if (dim == 0 && !(isfinite(lsum) && lsum > 0.0f)) flag_error(p.error_word, kErrNormalizer);
+                p.out[row * D + dim] = a / lsum;
+            }
+        } else {
+            const std::size_t slot = row * p.max_splits + split;
+            p.ws_o[slot * D + dim] = a;
+            if (dim == 0) {
+                p.ws_ml[slot * 2] = mw;
+                p.ws_ml[slot * 2 + 1] = lsum;
+            }
+        }
+    }
+    if (single) return;
+
+    // Fused split combine: the last CTA of this (sequence, kv-head) merges.
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        const std::uint32_t previous = atomicAdd(&p.ws_count[pair], 1u);
+        *flag = previous == static_cast<std::uint32_t>(nsplit - 1) ? 2 : 0;
+    }
+    __syncthreads();
+    if (*flag != 2) return;
+    __threadfence();
+    for (int i = threadIdx.x; i < GROUP * D; i += blockDim.x) {
+        const int h = i / D;
+        const int dim = i % D;
+        const std::size_t row = row0 + h;
+        const float* ml = p.ws_ml + row * p.max_splits * 2;
+        const float* o = p.ws_o + row * p.max_splits * D + dim;
+        float mw = -INFINITY;
+        for (int sp = 0; sp < nsplit; ++sp) mw = fmaxf(mw, __ldcg(ml + sp * 2));
+        const float base = safe_max(mw);
+        float lsum = 0.0f;
+        float a = 0.0f;
+        for (int sp = 0; sp < nsplit; ++sp) {
+            const float f = exp2f(__ldcg(ml + sp * 2) - base);
+            lsum += __ldcg(ml + sp * 2 + 1) * f;
+            a += __ldcg(o + static_cast<std::size_t>(sp) * D) * f;
+        }
+        if (p.emit_partials) {
+            p.part_o[row * D + dim] = a;
+            if (dim == 0) {
+                p.part_m[row] = mw * kLn2;
+                p.part_l[row] = lsum;
+            }
+        } else {
+            if (dim == 0 && !(isfinite(lsum) && lsum > 0.0f)) flag_error(p.error_word, kErrNormalizer);
+            p.out[row * D + dim] = a / lsum;
+        }
+    }
+    if (threadIdx.x == 0) p.ws_count[pair] = 0;
+}
+
+// K4: log-sum-exp merge of partials in part order; one warp per row.
+__global__ void lse_combine_kernel(const float* part_m, const float* part_l, const float* part_o,
+                                   std::uint32_t parts, std::uint64_t rows, std::uint32_t head_dim,
+                                   float* out) {
+    const std::uint64_t row = static_cast<std::uint64_t>(blockIdx.x) * (blockDim.x / 32) +
+                              threadIdx.x / 32;
+    const int lane = threadIdx.x & 31;
+    if (row >= rows) return;
+    float mw = -INFINITY;
+    for (std::uint32_t i = 0; i < parts; ++i) {
+        if (part_l[i * rows + row] > 0.0f) mw = fmaxf(mw, part_m[i * rows + row]);
+    }
+    float lsum = 0.0f;
+    for (std::uint32_t i = 0; i < parts; ++i) {
+        const float li = part_l[i * rows + row];
+        if (li > 0.0f) lsum += li * expf(part_m[i * rows + row] - mw);
+    }
+    for (std::uint32_t dim = lane; dim < head_dim; dim += 32) {
+        float a = 0.0f;
+        for (std::uint32_t i = 0; i < parts; ++i) {
+            if (part_l[i * rows + row] > 0.0f) {
+                a += part_o[(i * rows + row) * head_dim + dim] * expf(part_m[i * rows + row] - mw);
+            }
+        }
+        out[row * head_dim + dim] = a / lsum;
+    }
+}
+
+struct DecodePlan {
+    std::uint32_t blocks_per_split;
+    std::uint32_t max_splits;
+};
+
+DecodePlan plan_decode(std::uint32_t num_seqs, std::uint32_t kv_heads,
+                       std::uint32_t max_context_len) {
+    const std::uint32_t max_blocks =
+        (max_context_len + kDecodeBlockTokens - 1) / kDecodeBlockTokens;
+    std::uint32_t bps = 0;
+    if (const char* env = std::getenv("INFERLAB_DECODE_BLOCKS_PER_SPLIT")) {
+        bps = static_cast<std::uint32_t>(std::strtoul(env, nullptr, 10));
+    }
+    if (bps == 0) {
+        // Aim for about eight waves of two CTAs per SM across 148 SMs if every
+        // context were max_context_len long, with at least 8 blocks per split.
+        const std::uint64_t pairs = static_cast<std::uint64_t>(num_seqs) * kv_heads;
+        const std::uint64_t target = 148ull * 2 * 8;
+        std::uint64_t splits = (target + pairs - 1) / pairs;
+        splits = std::max<std::uint64_t>(1, std::min<std::uint64_t>(splits, max_blocks));
+        bps = static_cast<std::uint32_t>((max_blocks + splits - 1) / splits);
+        bps = std::max<std::uint32_t>(bps, 8);
+    }
+    bps = std::min<std::uint32_t>(std::max<std::uint32_t>(bps, 1), kMaxBlocksPerSplit);
+    const std::uint32_t max_splits = std::max<std::uint32_t>(1, (max_blocks + bps - 1) / bps);
+    return DecodePlan{bps, max_splits};
+}
+
+std::size_t workspace_bytes_for(std::uint32_t num_seqs, std::uint32_t q_heads,
+                                std::uint32_t kv_heads, std::uint32_t head_dim,
+                                const DecodePlan& plan) {
+    const std::size_t counters = (static_cast<std::size_t>(num_seqs) * kv_heads * 4 + 255) & ~std::size_t(255);
+    const std::size_t slots = static_cast<std::size_t>(num_seqs) * q_heads * plan.max_splits;
+    const std::size_t ml = (slots * 2 * 4 + 255) & ~std::size_t(255);
+    return counters + ml + slots * head_dim * 4;
+}
+
+using DecodeKernel = void (*)(const DecodeParams);
+
+template <typename KvT, int D>
+DecodeKernel pick_group(std::uint32_t group) {
+    switch (group) {
+        case 1: return paged_decode_kernel<KvT, D, 1>;
+        case 2: return paged_decode_kernel<KvT, D, 2>;
+        case 4: return paged_decode_kernel<KvT, D, 4>;
+        case 8: return paged_decode_kernel<KvT, D, 8>;
+        default: return nullptr;
+    }
+}
+
+template <typename KvT, int D>
+std::size_t smem_for_group(std::uint32_t group) {
+    switch (group) {
+        case 1: return DecodeSmem<KvT, D, 1>::kBytes;
+        case 2: return DecodeSmem<KvT, D, 2>::kBytes;
+        case 4: return DecodeSmem<KvT, D, 4>::kBytes;
+        case 8: return DecodeSmem<KvT, D, 8>::kBytes;
+        default: return 0;
+    }
+}
+
+template <typename KvT>
+DecodeKernel pick_kernel(std::uint32_t head_dim, std::uint32_t group, std::size_t& smem) {
+    if (head_dim == 64) {
+        smem = smem_for_group<KvT, 64>(group);
+        return pick_group<KvT, 64>(group);
+    }
+    if (head_dim == 128) {
+        smem = smem_for_group<KvT, 128>(group);
+        return pick_group<KvT, 128>(group);
+    }
+    return nullptr;
+}
+
+// The fast kernel covers block_tokens 16, head_dim 64/128 and GQA groups of
+// 1/2/4/8; other pool geometries use the generic CUDA-core kernel.
+DecodeKernel select_decode(const InferlabCudaKvPool& pool, std::uint32_t group, std::size_t& smem) {
+    if (pool.block_tokens != kDecodeBlockTokens) return nullptr;
+    if (pool.dtype == kFp32) return pick_kernel<float>(pool.head_dim, group, smem);
+    if (pool.dtype == kF16) return pick_kernel<__half>(pool.head_dim, group, smem);
+    return pick_kernel<__nv_bfloat16>(pool.head_dim, group, smem);
+}
+
+void validate_decode(const InferlabCudaKvPool& p, const float* queries,
+                     const std::int32_t* block_tables, std::uint32_t max_blocks,
+                     const std::int32_t* context_lens, std::uint32_t num_seqs,
+                     std::uint32_t q_heads, std::uint32_t max_context_len) {
+    if (queries == nullptr || block_tables == nullptr || context_lens == nullptr) {
+        throw std::runtime_error("paged decode pointer is null");
+    }
+    if (q_heads == 0 || q_heads % p.kv_heads != 0) {
+        throw std::runtime_error("paged decode q_heads must be a positive multiple of kv_heads");
+    }
+    if (max_blocks == 0 || max_context_len == 0) {
+        throw std::runtime_error("paged decode block table and context bound must be positive");
+    }
+    if (num_seqs > 0x7FFFFFFFu / std::max<std::uint32_t>(1, p.kv_heads)) {
+        throw std::runtime_error("paged decode batch is too large");
+    }
+}
+
+void run_decode(InferlabCudaKvPool& p, const float* queries, const std::int32_t* block_tables,
+                std::uint32_t max_blocks, const std::int32_t* context_lens, std::uint32_t num_seqs,
+                std::uint32_t q_heads, std::uint32_t max_context_len, float* out, float* part_m,
+                float* part_l, float* part_o, void* workspace, std::size_t workspace_bytes,
+                cudaStream_t stream) {
+    const std::uint32_t group = q_heads / p.kv_heads;
+    std::size_t smem = 0;
+    DecodeKernel kernel = select_decode(p, group, smem);
+    if (kernel == nullptr) {
+        // Generic CUDA-core path (any head_dim / block size / group).
+        if (part_m != nullptr) {
+            throw std::runtime_error(
+                "paged decode partials need block_tokens 16, head_dim 64 or 128 and a GQA group of 1, 2, 4 or 8");
+        }
+        if (p.head_dim > kGenericMaxHeadDim) {
+            throw std::runtime_error("attention head_dimension exceeds the CUDA kernel limit of 4096");
+        }
+        GenericParams g{};
+        g.queries = queries;
+        g.query_precision = p.dtype;
+        g.out = out;
+        g.query_rows = num_seqs;
+        g.q_heads = q_heads;
+        g.kv_heads = p.kv_heads;
+        g.head_dim = p.head_dim;
+        g.scale = 1.0f / std::sqrt(static_cast<float>(p.head_dim));
+        g.error_word = p.error_word;
+        g.check_normalizer = 1;
+        SegmentMap seg{};
+        seg.mode = 1;
+        seg.context_lens = context_lens;
+        seg.max_kv = std::min<long long>(max_context_len,
+                                         static_cast<long long>(max_blocks) * p.block_tokens);
+        const std::size_t gsmem = generic_smem_bytes(p.head_dim);
+        const unsigned grid = static_cast<unsigned>(
+            (static_cast<std::size_t>(num_seqs) * q_heads + kGenericWarps - 1) / kGenericWarps);
+        auto launch = [&](auto kv) {
+            auto* fn = generic_attention_kernel<decltype(kv)>;
+            cuda_check(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                            static_cast<int>(gsmem)),
+                       "cudaFuncSetAttribute");
+            fn<<<grid, kGenericWarps * 32, gsmem, stream>>>(g, kv, seg);
+        };
+        if (p.dtype == kFp32) {
+            launch(PagedKv<float>{static_cast<const float*>(p.key_arena),
+                                  static_cast<const float*>(p.value_arena), block_tables,
+                                  max_blocks, p.block_tokens, p.kv_heads, p.head_dim,
+                                  p.num_blocks, p.error_word});
+        } else if (p.dtype == kF16) {
+            launch(PagedKv<__half>{static_cast<const __half*>(p.key_arena),
+                                   static_cast<const __half*>(p.value_arena), block_tables,
+                                   max_blocks, p.block_tokens, p.kv_heads, p.head_dim,
+                                   p.num_blocks, p.error_word});
+        } else {
+            launch(PagedKv<__nv_bfloat16>{static_cast<const __nv_bfloat16*>(p.key_arena),
+                                          static_cast<const __nv_bfloat16*>(p.value_arena),
+                                          block_tables, max_blocks, p.block_tokens, p.kv_heads,
+                                          p.head_dim, p.num_blocks, p.error_word});
+        }
+        cuda_check(cudaGetLastError(), "generic decode launch");
+        return;
+    }
+    if (reinterpret_cast<std::uintptr_t>(queries) % 16 != 0) {
+        throw std::runtime_error("paged decode queries must be 16-byte aligned");
+    }
+    const DecodePlan plan = plan_decode(num_seqs, p.kv_heads, max_context_len);
+    const std::size_t need = workspace_bytes_for(num_seqs, q_heads, p.kv_heads, p.head_dim, plan);
+    if (plan.max_splits > 1 && (workspace == nullptr || workspace_bytes < need)) {
+        throw std::runtime_error("paged decode workspace is too small");
+    }
+    DecodeParams d{};
+    d.key_arena = static_cast<const unsigned char*>(p.key_arena);
+    d.value_arena = static_cast<const unsigned char*>(p.value_arena);
+    d.num_blocks = p.num_blocks;
+    d.kv_heads = p.kv_heads;
+    d.queries = queries;
+    d.q_heads = q_heads;
+    d.tables = block_tables;
+    d.max_blocks = max_blocks;
+    d.context_lens = context_lens;
+    d.max_context = max_context_len;
+    d.blocks_per_split = plan.blocks_per_split;
+    d.max_splits = plan.max_splits;
+    d.scale_log2 = (1.0f / std::sqrt(static_cast<float>(p.head_dim))) * kLog2e;
+    d.emit_partials = part_m != nullptr ? 1 : 0;
+    d.out = out;
+    d.part_m = part_m;
+    d.part_l = part_l;
+    d.part_o = part_o;
+    if (workspace != nullptr) {
+        auto* base = static_cast<unsigned char*>(workspace);
+        const std::size_t counters =
+            (static_cast<std::size_t>(num_seqs) * p.kv_heads * 4 + 255) & ~std::size_t(255);
+        const std::size_t slots = static_cast<std::size_t>(num_seqs) * q_heads * plan.max_splits;
+        const std::size_t ml = (slots * 2 * 4 + 255) & ~std::size_t(255);
+        d.ws_count = reinterpret_cast<std::uint32_t*>(base);
+        d.ws_ml = reinterpret_cast<float*>(base + counters);
+        d.ws_o = reinterpret_cast<float*>(base + counters + ml);
+    }
+    d.error_word = p.error_word;
+    cuda_check(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    static_cast<int>(smem)),
+               "cudaFuncSetAttribute");
+    const std::uint64_t grid = static_cast<std::uint64_t>(num_seqs) * p.kv_heads * plan.max_splits;
+    if (grid > 0x7FFFFFFFull) throw std::runtime_error("paged decode grid is too large");
+    kernel<<<static_cast<unsigned>(grid), kDecodeWarps * 32, smem, stream>>>(d);
+    cuda_check(cudaGetLastError(), "paged decode launch");
+}
+
+}  // namespace
+}  // namespace ilb
+
+extern "C" std::size_t inferlab_cuda_paged_decode_workspace_size(const InferlabCudaKvPool* pool,
+                                                                 std::uint32_t num_seqs,
+                                                                 std::uint32_t q_heads,
+                                                                 std::uint32_t max_context_len) {
+    if (pool == nullptr || num_seqs == 0 || q_heads == 0 || max_context_len == 0) return 0;
+    const auto plan = ilb::plan_decode(num_seqs, pool->kv_heads, max_context_len);
+    return ilb::workspace_bytes_for(num_seqs, q_heads, pool->kv_heads, pool->head_dim, plan);
+}
+
+extern "C" int inferlab_cuda_paged_decode_workspace_init(void* workspace,
+                                                         std::size_t workspace_bytes,
+                                                         void* stream, char* error,
+                                                         std::size_t error_capacity) {
+    return ilb::protect(error, error_capacity, [&] {
+        if (workspace == nullptr || workspace_bytes == 0) return;
+        ilb::cuda_check(cudaMemsetAsync(workspace, 0, workspace_bytes,
+                                        static_cast<cudaStream_t>(stream)),
+                        "cudaMemsetAsync workspace");
+    });
+}
+
+extern "C" int inferlab_cuda_paged_decode(InferlabCudaKvPool* pool, const float* queries,
+                                          const std::int32_t* block_tables,
+                                          std::uint32_t max_blocks_per_seq,
+                                          const std::int32_t* context_lens, std::uint32_t num_seqs,
+                                          std::uint32_t q_heads, std::uint32_t max_context_len,
+                                          float* out, void* workspace, std::size_t workspace_bytes,
+                                          void* stream, char* error, std::size_t error_capacity) {
+    return ilb::protect(error, error_capacity, [&] {
+        using namespace ilb;
+        auto& p = checked_pool(pool);
+        if (num_seqs == 0) return;
+        validate_decode(p, queries, block_tables, max_blocks_per_seq, context_lens, num_seqs,
+                        q_heads, max_context_len);
+        if (out == nullptr) throw std::runtime_error("paged decode output pointer is null");
+        DeviceGuard guard(p.device);
+        run_decode(p, queries, block_tables, max_blocks_per_seq, context_lens, num_seqs, q_heads,
+                   max_context_len, out, nullptr, nullptr, nullptr, workspace, workspace_bytes,
+                   static_cast<cudaStream_t>(stream));
+    });
+}
+
+extern "C" int inferlab_cuda_paged_decode_partials(
+    InferlabCudaKvPool* pool, const float* queries, const std::int32_t* block_tables,
+    std::uint32_t max_blocks_per_seq, const std::int32_t* context_lens, std::uint32_t num_seqs,
+    std::uint32_t q_heads, std::uint32_t max_context_len, float* part_m, float* part_l,
+    float* part_o, void* workspace, std::size_t workspace_bytes, void* stream, char* error,
+    std::size_t error_capacity) {
+    return ilb::protect(error, error_capacity, [&] {
+        using namespace ilb;
+        auto& p = checked_pool(pool);
+        if (num_seqs == 0) return;
+        validate_decode(p, queries, block_tables, max_blocks_per_seq, context_lens, num_seqs,
+                        q_heads, max_context_len);
+        if (part_m == nullptr || part_l == nullptr || part_o == nullptr) {
+            throw std::runtime_error("paged decode partial output pointer is null");
+        }
+        DeviceGuard guard(p.device);
+        run_decode(p, queries, block_tables, max_blocks_per_seq, context_lens, num_seqs, q_heads,
+                   max_context_len, nullptr, part_m, part_l, part_o, workspace, workspace_bytes,
+                   static_cast<cudaStream_t>(stream));
+    });
+}
+
+extern "C" int inferlab_cuda_lse_combine(const float* part_m, const float* part_l,
+                                         const float* part_o, std::uint32_t parts,
+                                         std::uint64_t rows, std::uint32_t head_dim, float* out,
+                                         void* stream, char* error, std::size_t error_capacity) {
+    return ilb::protect(error, error_capacity, [&] {
+        if (rows == 0) return;
+        if (part_m == nullptr || part_l == nullptr || part_o == nullptr || out == nullptr) {
+            throw std::runtime_error("lse combine pointer is null");
+        }
+        if (parts == 0 || head_dim == 0) {
+            throw std::runtime_error("lse combine parts and head_dim must be positive");
+        }
+        const std::uint64_t blocks = (rows + 3) / 4;
+        if (blocks > 0x7FFFFFFFull) throw std::runtime_error("lse combine is too large");
+        ilb::lse_combine_kernel<<<static_cast<unsigned>(blocks), 128, 0,
+                                  static_cast<cudaStream_t>(stream)>>>(part_m, part_l, part_o,
+                                                                       parts, rows, head_dim, out);
+        ilb::cuda_check(cudaGetLastError(), "lse combine launch");
+    });
+}

@@ -1,0 +1,43 @@
+// pool.cuh - the HBM-resident paged KV pool shared by the append, gather,
+// decode and prefill kernels.
+#pragma once
+
+#include "common.cuh"
+
+#include <mutex>
+
+struct InferlabCudaKvPool {
+    int device = 0;
+    std::uint32_t dtype = 0;
+    std::uint32_t element_bytes = 4;
+    std::uint32_t block_tokens = 16;
+    std::uint32_t kv_heads = 1;
+    std::uint32_t head_dim = 1;
+    std::uint64_t num_blocks = 0;
+    std::uint64_t block_bytes = 0;  // one block, all kv-heads, one arena
+    std::uint64_t arena_bytes = 0;
+    void* key_arena = nullptr;
+    void* value_arena = nullptr;
+    std::uint32_t* error_word = nullptr;       // device
+    std::uint32_t* error_host = nullptr;       // pinned mirror
+    std::mutex mutex;                          // guards error_host / error readback
+};
+
+namespace ilb {
+
+inline InferlabCudaKvPool& checked_pool(InferlabCudaKvPool* pool) {
+    if (pool == nullptr) throw std::runtime_error("paged KV pool pointer is null");
+    return *pool;
+}
+
+inline const InferlabCudaKvPool& checked_pool(const InferlabCudaKvPool* pool) {
+    if (pool == nullptr) throw std::runtime_error("paged KV pool pointer is null");
+    return *pool;
+}
+
+// Bytes of one kv-head's block tile in one arena.
+inline std::size_t head_tile_bytes(const InferlabCudaKvPool& pool) {
+    return static_cast<std::size_t>(pool.block_tokens) * pool.head_dim * pool.element_bytes;
+}
+
+}  // namespace ilb
