@@ -89,7 +89,7 @@ class ClockSampler:
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.device_id}", f"--query-gpu={self.FIELDS}",
-                 "--format=csv,noheader,nounits", "-lms", "100"],
+                 "--format=csv,noheader,nounits", "-lms", "20"],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.reader = threading.Thread(target=self._read, daemon=True)
             self.reader.start()
@@ -245,21 +245,32 @@ def run_ours(args):
         flush.fill_(float(i))
         step()
     pool.synchronize()
+    # Clock samples: a ~0.5 s untimed pre-roll of the same step, the timed
+    # steps and the e2e steps (the timed region alone is a few milliseconds,
+    # shorter than nvidia-smi's sampling interval).
+    clocks = ClockSampler(device).__enter__()
+    preroll_end = time.perf_counter() + 0.5
+    while time.perf_counter() < preroll_end:
+        flush.fill_(0.0)
+        step()
+        stream.synchronize()
 
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     barrier(dist)
     torch.cuda.synchronize(device)
-    with ClockSampler(device) as clocks:
-        wall0 = time.perf_counter()
-        for i in range(args.steps):
-            flush.fill_(float(i))  # evict the previous step's K/V from L2
-            starts[i].record(stream)
-            step()
-            ends[i].record(stream)
-        torch.cuda.synchronize(device)
-        wall = time.perf_counter() - wall0
-        barrier(dist)
+    wall0 = time.perf_counter()
+    # Keep the GPU busy while the host enqueues every timed step, so the step
+    # events time the kernels and not the host's launch latency.
+    torch.cuda._sleep(int(2e6 + 3e5 * args.steps))
+    for i in range(args.steps):
+        flush.fill_(float(i))  # evict the previous step's K/V from L2
+        starts[i].record(stream)
+        step()
+        ends[i].record(stream)
+    torch.cuda.synchronize(device)
+    wall = time.perf_counter() - wall0
+    barrier(dist)
     pool.synchronize()
     kernel_ms = sum(s.elapsed_time(e) for s, e in zip(starts, ends))
     total_ms = max_over_ranks(dist, kernel_ms)
@@ -270,12 +281,14 @@ def run_ours(args):
     peak = float(peaks["hbm_gbs"])
 
     e2e = run_decode_e2e(args, batch, pool, workspace, flush, device, dist, bytes_per_step)
+    clocks.__exit__(None, None, None)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu = cpu_baseline_decode(batch, bytes_per_step, args.cpu_seconds)
 
     clock = clocks.summary()
+    clock["window"] = "0.5 s pre-roll of the same step + timed steps + e2e steps"
     line = {
         "metric": "decode attn KV-bytes GB/s",
         "value": round(value, 3),
@@ -434,6 +447,12 @@ def run_prefill(args, dist, world, rank, device, peaks, peak_kind):
     barrier(dist)
     torch.cuda.synchronize(device)
     with ClockSampler(device) as clocks:
+        preroll_end = time.perf_counter() + 0.5
+        while time.perf_counter() < preroll_end:
+            flush.fill_(0.0)
+            step()
+            stream.synchronize()
+        torch.cuda._sleep(int(2e6 + 3e5 * args.steps))
         for i in range(args.steps):
             flush.fill_(float(i))
             starts[i].record(stream)

@@ -175,11 +175,9 @@ inferlab::AttentionConfig map_config(std::uint32_t algorithm, std::uint32_t prec
 namespace inferlab {
 
 float round_attention_value(float value, AttentionPrecision precision) {
-    // Host-side storage rounding with the same semantics as the device path:
-    // IEEE round to nearest even (kernels/attention_cpu.cpp:405-417).
-    if (precision == AttentionPrecision::Fp32) return value;
-    if (precision == AttentionPrecision::Fp16) return __half2float(__float2half_rn(value));
-    return __bfloat162float(__float2bfloat16_rn(value));
+    // The reference's storage simulation, including its widening of fp16
+    // subnormals to half their value (see round_reference).
+    return ilb::round_reference(value, static_cast<std::uint32_t>(precision));
 }
 
 void attention_forward(const float* queries, const float* keys, const float* values,
@@ -254,6 +252,7 @@ void attention_forward(const float* queries, const float* keys, const float* val
     GenericParams params{};
     params.queries = d_q;
     params.query_precision = static_cast<std::uint32_t>(config.precision);
+    params.reference_rounding = 1;
     params.out = d_out;
     params.query_rows = static_cast<long long>(query_tokens);
     params.q_heads = static_cast<std::uint32_t>(heads);

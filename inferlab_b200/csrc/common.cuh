@@ -113,6 +113,23 @@ __device__ __forceinline__ float round_storage(float x, std::uint32_t precision)
     return x;
 }
 
+// The reference's own storage simulation, round_attention_value
+// (kernels/attention_cpu.cpp:405-417), used by the drop-in entry so that its
+// Fp16 mode matches the reference bit for bit. It differs from IEEE in one
+// place: half_bits_to_float (kernels/attention_cpu.cpp:76-89) builds the
+// exponent of an fp16 subnormal as 127 - 15 - shift, one below the exact
+// 127 - 14 - shift, so every value that rounds to an fp16 subnormal
+// (|x| < 2^-14) comes back at half its value. The paged pool stores real
+// fp16 numbers and widens them exactly (round_storage / Storage<__half>).
+__host__ __device__ __forceinline__ float round_reference(float x, std::uint32_t precision) {
+    if (precision == kF16) {
+        const float widened = __half2float(__float2half_rn(x));
+        return fabsf(widened) < 6.103515625e-05f ? widened * 0.5f : widened;
+    }
+    if (precision == kBf16) return __bfloat162float(__float2bfloat16_rn(x));
+    return x;
+}
+
 template <typename T>
 struct Storage;
 template <>

@@ -43,7 +43,7 @@ struct ContiguousKv {
         return Row{values + (static_cast<std::size_t>(token) * heads + head) * head_dim};
     }
     __device__ __forceinline__ float load(const Row& row, std::uint32_t dim) const {
-        return round_storage(row.ptr[dim], precision);
+        return round_reference(row.ptr[dim], precision);
     }
 };
 
@@ -147,6 +147,7 @@ struct SegmentMap {
 struct GenericParams {
     const float* queries;  // [rows / heads][q_heads][head_dim]
     std::uint32_t query_precision;
+    int reference_rounding;  // 1: round_reference (drop-in entry), 0: round_storage
     float* out;
     long long query_rows;  // number of query tokens
     std::uint32_t q_heads;
@@ -200,7 +201,8 @@ __global__ void __launch_bounds__(kGenericWarps * 32)
 
     const float* q_global = p.queries + static_cast<std::size_t>(row) * d;
     for (unsigned c = lane; c < d; c += 32) {
-        q_s[c] = round_storage(q_global[c], p.query_precision);
+        q_s[c] = p.reference_rounding ? round_reference(q_global[c], p.query_precision)
+                                      : round_storage(q_global[c], p.query_precision);
         acc_s[c] = 0.0f;
     }
     __syncwarp();
@@ -217,8 +219,14 @@ __global__ void __launch_bounds__(kGenericWarps * 32)
             if (token < legal) {
                 const auto krow = kv.key_row(segment, token, kv_head);
                 float s = 0.0f;
-                for (unsigned c = 0; c < d; ++c) s = fmaf(q_s[c], kv.load(krow, c), s);
-                score[j] = s * p.scale;
+                // Same order and rounding as the reference's dot product
+                // (kernels/attention_cpu.cpp:245-251): sequential over the
+                // head dimension, product and sum rounded separately, so the
+                // scores - whose errors exp() amplifies - agree exactly.
+                for (unsigned c = 0; c < d; ++c) {
+                    s = __fadd_rn(s, __fmul_rn(q_s[c], kv.load(krow, c)));
+                }
+                score[j] = __fmul_rn(s, p.scale);
                 chunk_max = fmaxf(chunk_max, score[j]);
             }
         }

@@ -100,7 +100,12 @@ uint16_t oracle_float_to_half_bits(float value) {
     return (uint16_t)(sign | result);
 }
 
-/* binary16 -> binary32, exact. Follows kernels/attention_cpu.cpp:69-97. */
+/* binary16 -> binary32 as the reference does it (kernels/attention_cpu.cpp:69-97).
+ * Its subnormal branch builds the exponent as 127 - 15 - shift (:86-88), one
+ * below the exact 127 - 14 - shift, so fp16 subnormals come back at half
+ * their value; restated as is, because round_attention_value depends on it
+ * and the parity target is the reference's behaviour. Normal numbers, zero
+ * and infinities are exact. */
 float oracle_half_bits_to_float(uint16_t half) {
     const uint32_t sign = ((uint32_t)half & 0x8000u) << 16;
     const uint32_t exponent = ((uint32_t)half >> 10) & 0x1Fu;
@@ -128,6 +133,18 @@ float oracle_half_bits_to_float(uint16_t half) {
 uint16_t oracle_float_to_bf16_bits(float value) {
     const uint32_t bits = float_bits(value);
     return (uint16_t)((bits + 0x7FFFu + ((bits >> 16) & 1u)) >> 16);
+}
+
+/* Exact binary16 -> binary32 (IEEE), for values that are stored as real fp16
+ * in the device pool: a subnormal h is h.fraction * 2^-24. */
+float oracle_half_bits_to_float_ieee(uint16_t half) {
+    const uint32_t exponent = ((uint32_t)half >> 10) & 0x1Fu;
+    const uint32_t fraction = (uint32_t)half & 0x3FFu;
+    if (exponent == 0) {
+        const float magnitude = (float)fraction * 5.9604644775390625e-08f; /* 2^-24 */
+        return (half & 0x8000u) ? -magnitude : magnitude;
+    }
+    return oracle_half_bits_to_float(half);
 }
 
 float oracle_bf16_bits_to_float(uint16_t bits) {
@@ -454,12 +471,13 @@ done:
 static float arena_value(const void* arena, uint32_t dtype, size_t index) {
     if (dtype == ORACLE_FP32) return ((const float*)arena)[index];
     const uint16_t bits = ((const uint16_t*)arena)[index];
-    return dtype == ORACLE_FP16 ? oracle_half_bits_to_float(bits) : oracle_bf16_bits_to_float(bits);
+    return dtype == ORACLE_FP16 ? oracle_half_bits_to_float_ieee(bits)
+                                : oracle_bf16_bits_to_float(bits);
 }
 
 /*
  * Gather `tokens` rows of one sequence into contiguous [tokens][kv_heads][head_dim]
- * fp32 (16-bit stored values widened exactly). Restates PagedKvPool::materialize
+ * fp32 (16-bit stored values widened exactly, IEEE, including fp16 subnormals). Restates PagedKvPool::materialize
  * (worker/cpp/inferlab_runtime.cpp:769-803): the table length must equal
  * ceil(tokens / block_tokens) (:776-780), ids must be in range (:931-936).
  */

@@ -89,6 +89,10 @@ def oracle_lib() -> ctypes.CDLL:
                 _f32p, _f32p, _f32p, _sz, _sz, _sz, _sz, _sz, _u32p, _f32p, _sz, _u64p,
                 ctypes.c_char_p, _sz,
             ]
+            lib.oracle_half_bits_to_float.restype = ctypes.c_float
+            lib.oracle_half_bits_to_float.argtypes = [ctypes.c_uint16]
+            lib.oracle_half_bits_to_float_ieee.restype = ctypes.c_float
+            lib.oracle_half_bits_to_float_ieee.argtypes = [ctypes.c_uint16]
             lib.oracle_round_value.restype = ctypes.c_float
             lib.oracle_round_value.argtypes = [ctypes.c_float, ctypes.c_uint32]
             lib.oracle_float_to_half_bits.restype = ctypes.c_uint16
@@ -125,6 +129,11 @@ def ref_lib() -> ctypes.CDLL | None:
                 ctypes.POINTER(InferlabAttentionConfig), _f32p, _sz,
                 ctypes.POINTER(InferlabAttentionStats), ctypes.c_char_p, _sz,
             ]
+            # C++ inferlab::round_attention_value(float, AttentionPrecision)
+            fn = getattr(lib, "_ZN8inferlab21round_attention_valueEfNS_18AttentionPrecisionE")
+            fn.restype = ctypes.c_float
+            fn.argtypes = [ctypes.c_float, ctypes.c_uint32]
+            lib.round_attention_value = fn
             _ref = lib
     return _ref
 
@@ -172,7 +181,21 @@ def attention_forward(q, k, v, q_tokens, kv_tokens, heads, head_dim, start=0,
 
 
 def round_values(values: np.ndarray, precision: int) -> np.ndarray:
-    """Storage rounding of every element (kernels/attention_cpu.cpp:405-417)."""
+    """The reference's storage rounding of every element
+    (round_attention_value, kernels/attention_cpu.cpp:405-417), including its
+    widening of fp16 subnormals to half their value (:86-88)."""
+    values = np.ascontiguousarray(values, dtype=np.float32)
+    if precision == FP32:
+        return values.copy()
+    if precision == FP16:
+        widened = half_bits_to_float(float_to_half_bits(values))
+        return np.where(np.abs(widened) < np.float32(2.0**-14), widened * np.float32(0.5),
+                        widened).astype(np.float32)
+    return bf16_bits_to_float(float_to_bf16_bits(values))
+
+
+def round_values_ieee(values: np.ndarray, precision: int) -> np.ndarray:
+    """IEEE round-to-nearest-even storage rounding (what the device pool stores)."""
     values = np.ascontiguousarray(values, dtype=np.float32)
     if precision == FP32:
         return values.copy()

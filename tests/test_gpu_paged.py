@@ -171,7 +171,7 @@ def test_append_then_gather_bit_exact(torch_mod, wl, oracle_mod):
             # the stored values are the rows rounded like round_attention_value
             mine = [i for i, r in enumerate(rows) if r[0] == s]
             order = np.argsort(pos[mine])
-            expect_k = oracle_mod.round_values(k_rows[mine][order], dtype)
+            expect_k = oracle_mod.round_values_ieee(k_rows[mine][order], dtype)
             assert np.array_equal(kg, expect_k)
         pool.close()
 
