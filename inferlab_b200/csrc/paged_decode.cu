@@ -223,7 +223,9 @@ __global__ void __launch_bounds__(kDecodeWarps * 32)
     int consumed = 0;
     for (int j = 0; j < my_count; ++j) {
         const int stage = j % kDecodeStages;
-        if (!mbar_wait_bounded(&my_bars[stage], (j / kDecodeStages) & 1, p.error_word)) {
+        // Warp-uniform outcome: the shuffles below need every lane.
+        if (!__all_sync(0xffffffffu,
+                        mbar_wait_bounded(&my_bars[stage], (j / kDecodeStages) & 1, p.error_word))) {
             *flag = 1;
             break;
         }

@@ -184,6 +184,10 @@ __host__ __device__ constexpr std::uint32_t idesc_f16(std::uint32_t a_type, std:
            ((128u >> 4) << 24);
 }
 
+// Warp-uniform outcome, so that no lane reaches a warp-collective TMEM load
+// (tcgen05.ld .sync.aligned) without the others.
+__device__ __forceinline__ bool warp_ok(bool ok) { return __all_sync(0xffffffffu, ok); }
+
 struct Waiter {
     int* abort;
     std::uint32_t* error_word;
@@ -369,7 +373,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         bool ok = true;
         for (int j = 0; j < n_tiles; ++j) {
             const int st = j & 1;
-            if (!(ok = wait(&bars[kBarS + st], (j >> 1) & 1))) break;
+            if (!(ok = warp_ok(wait(&bars[kBarS + st], (j >> 1) & 1)))) break;
             tc_fence_after();
             const int key0 = j * kBN;
             const bool full = key0 + kBN - 1 <= start + q_lo;  // no masking anywhere in the tile
@@ -389,7 +393,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             const float base = m_new == -INFINITY ? 0.0f : m_new;
             const float alpha = exp2f(m - base);
             if (j > 0) {
-                if (!(ok = wait(&bars[kBarPV], (j - 1) & 1))) break;
+                if (!(ok = warp_ok(wait(&bars[kBarPV], (j - 1) & 1)))) break;
                 tc_fence_after();
 #pragma unroll
                 for (int c = 0; c < 4; ++c) {
@@ -402,7 +406,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             if constexpr (kBf16) {
                 // V arrived as bf16; PV runs with fp16 operands (P needs fp16's
                 // 11-bit significand), so widen V in place: same 16-bit layout.
-                if (!(ok = wait(&bars[kBarV + st], (j >> 1) & 1))) break;
+                if (!(ok = warp_ok(wait(&bars[kBarV + st], (j >> 1) & 1)))) break;
                 uint4* v = reinterpret_cast<uint4*>(smem + kV0 + st * kTile);
                 for (int i = row; i < kTile / 16; i += 128) {
                     uint4 w = v[i];
@@ -453,15 +457,19 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_arrive(&bars[kBarSFree + st]);
             mbar_arrive(&bars[kBarP]);
         }
-        if (ok && wait(&bars[kBarPV], (n_tiles - 1) & 1)) {
+        if (ok && warp_ok(wait(&bars[kBarPV], (n_tiles - 1) & 1))) {
             tc_fence_after();
             const float inv = 1.0f / l;
-            if (row < rows) {
-                float* out = p.out + (static_cast<std::size_t>(offset + q_lo + row) * p.q_heads + head) * kD;
+            // Every lane takes part in the TMEM loads (warp-collective); only
+            // rows inside the segment store.
+            const bool store = row < rows;
+            float* out = p.out + (static_cast<std::size_t>(offset + q_lo + (store ? row : 0)) *
+                                      p.q_heads + head) * kD;
 #pragma unroll
-                for (int c = 0; c < 4; ++c) {
-                    float pv[32];
-                    tmem_load32(lane_addr + 256 + c * 32, pv);
+            for (int c = 0; c < 4; ++c) {
+                float pv[32];
+                tmem_load32(lane_addr + 256 + c * 32, pv);
+                if (store) {
 #pragma unroll
                     for (int i = 0; i < 32; i += 4) {
                         float4 w;
@@ -472,13 +480,14 @@ __global__ void __launch_bounds__(kThreads, 1)
                         *reinterpret_cast<float4*>(out + c * 32 + i) = w;
                     }
                 }
-                if (!(isfinite(l) && l > 0.0f)) flag_error(p.error_word, kErrNormalizer);
             }
+            if (store && !(isfinite(l) && l > 0.0f)) flag_error(p.error_word, kErrNormalizer);
         }
     }
     tc_fence_before();
     __syncthreads();
     if (warp == 5) {
+        __syncwarp();
         tc_fence_after();
         tmem_dealloc(tmem, kTmemCols);
     }

@@ -45,6 +45,16 @@ def oracle_prefill(oracle_mod, wl, batch):
                                       batch.q_heads)
 
 
+def test_tc_prefill_single_tile(wl, oracle_mod):
+    """One 128-query tile of one head: the smallest tensor-core case."""
+    batch = wl.prefill_batch(0, 51, [0], [128], 1, 1, 128, 1, 0.5)
+    out = batch.pool.prefill(batch.prefill_queries, batch.prefill_tables, batch.starts_dev,
+                             batch.counts_dev, batch.offsets_dev, 128)
+    batch.pool.synchronize()
+    check_f16(out.cpu().numpy(), oracle_prefill(oracle_mod, wl, batch))
+    batch.pool.close()
+
+
 @pytest.mark.parametrize("dtype", [1, 2])
 def test_tc_prefill_ragged_chunks(wl, oracle_mod, dtype):
     """Full prompts and chunks with prior context, lengths off the 16/128 grid."""
