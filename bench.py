@@ -227,6 +227,10 @@ def run_ours(args):
 
     if args.workload == "prefill_f16":
         return run_prefill(args, dist, world, rank, device, peaks, peak_kind)
+    if args.workload == "mixed_bf16":
+        return run_mixed(args, dist, world, rank, device, peaks, peak_kind)
+    if args.workload == "longseq_split":
+        return run_long_sequence(args, dist, world, rank, device, peaks, peak_kind)
 
     batch, desc, dtype_name, scaling = build_decode(args.workload, rank, world, device)
     pool = batch.pool
@@ -323,46 +327,31 @@ def run_ours(args):
 
 
 def run_decode_e2e(args, batch, pool, workspace, flush, device, dist, bytes_per_step):
-    """The same step through the host-facing API with host buffers: per step,
-    copy from pinned host memory the queries, the new token's K/V rows, the
-    block tables and context lengths, append the new rows (kv_append at
-    position ctx - 1), decode, and copy the output back; host wall clock
-    around all of it (stream synchronised at the end of every step)."""
+    """The same decode step through the C ABI with HOST buffers: one
+    inferlab_cuda_decode_step_host call per step takes the step's queries,
+    the new token's K/V rows, the block tables and context lengths from host
+    memory, copies them to HBM through the pool's pinned staging, appends the
+    new rows at position ctx - 1, decodes every sequence and copies the output
+    back (synchronous). Host wall clock around each call."""
     import torch
 
     num_seqs, q_heads, head_dim = batch.queries.shape
     kvh = batch.kv_heads
-    pin = dict(pin_memory=True)
     gen = np.random.Generator(np.random.PCG64(99))
-    h_q = torch.from_numpy(gen.standard_normal((num_seqs, q_heads, head_dim), dtype=np.float32)).pin_memory()
-    h_k = torch.from_numpy(gen.standard_normal((num_seqs, kvh, head_dim), dtype=np.float32)).pin_memory()
-    h_v = torch.from_numpy(gen.standard_normal((num_seqs, kvh, head_dim), dtype=np.float32)).pin_memory()
-    h_tables = torch.from_numpy(batch.tables_host).pin_memory()
-    h_lens = torch.from_numpy(batch.contexts.astype(np.int32)).pin_memory()
-    h_pos = torch.from_numpy((batch.contexts - 1).astype(np.int32)).pin_memory()
-    h_seq = torch.arange(num_seqs, dtype=torch.int32).pin_memory()
-    h_out = torch.empty((num_seqs, q_heads, head_dim), dtype=torch.float32, **pin)
-    dev = f"cuda:{device}"
-    d_q = torch.empty_like(h_q, device=dev)
-    d_k = torch.empty_like(h_k, device=dev)
-    d_v = torch.empty_like(h_v, device=dev)
-    d_tables = torch.empty_like(h_tables, device=dev)
-    d_lens = torch.empty_like(h_lens, device=dev)
-    d_pos = torch.empty_like(h_pos, device=dev)
-    d_seq = torch.empty_like(h_seq, device=dev)
-    d_out = torch.empty_like(h_out, device=dev)
-    h2d = sum(t.numel() * t.element_size() for t in (h_q, h_k, h_v, h_tables, h_lens, h_pos, h_seq))
-    d2h = h_out.numel() * h_out.element_size()
+    h_q = gen.standard_normal((num_seqs, q_heads, head_dim), dtype=np.float32)
+    h_k = gen.standard_normal((num_seqs, kvh, head_dim), dtype=np.float32)
+    h_v = gen.standard_normal((num_seqs, kvh, head_dim), dtype=np.float32)
+    h_tables = np.ascontiguousarray(batch.tables_host, dtype=np.int32)
+    h_lens = batch.contexts.astype(np.int32)
+    h_out = np.empty((num_seqs, q_heads, head_dim), dtype=np.float32)
+    # payload crossing the bus each step: inputs (+ positions and sequence ids
+    # derived on the host) down, output + error word up
+    h2d = (h_q.nbytes + h_k.nbytes + h_v.nbytes + h_tables.nbytes + 3 * h_lens.nbytes)
+    d2h = h_out.nbytes + 4
     stream = torch.cuda.current_stream(device)
 
     def step():
-        for d, h in ((d_q, h_q), (d_k, h_k), (d_v, h_v), (d_tables, h_tables), (d_lens, h_lens),
-                     (d_pos, h_pos), (d_seq, h_seq)):
-            d.copy_(h, non_blocking=True)
-        pool.append(d_k, d_v, d_seq, d_pos, d_tables)
-        pool.decode(d_q, d_tables, d_lens, batch.max_context_len, out=d_out, workspace=workspace)
-        h_out.copy_(d_out, non_blocking=True)
-        stream.synchronize()
+        pool.decode_step_host(h_q, h_tables, h_lens, h_k, h_v, out=h_out, stream=stream)
 
     for i in range(args.warmup):
         flush.fill_(float(i))
@@ -384,8 +373,8 @@ def run_decode_e2e(args, batch, pool, workspace, flush, device, dist, bytes_per_
             "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
             "ms_per_step": round(total / args.steps * 1e3, 5),
             "gpu_launches_per_step": 2,
-            "path": "pinned H2D of q/new K,V rows/tables/lengths -> inferlab_cuda_kv_append -> "
-                    "inferlab_cuda_paged_decode -> D2H of the output, host wall clock"}
+            "path": "inferlab_cuda_decode_step_host: host arrays -> pinned staging -> one H2D, "
+                    "kv_append, paged decode, one D2H; host wall clock per call"}
 
 
 def host_threads() -> int:
@@ -492,6 +481,142 @@ def run_prefill(args, dist, world, rank, device, peaks, peak_kind):
 # ---------------------------------------------------------------------------
 # reference arm
 # ---------------------------------------------------------------------------
+def _timed_steps(args, dist, device, stream, flush, parts):
+    """Runs `parts` (list of callables) per step after a GPU sleep, each part
+    bracketed by its own events; returns per-part total ms (this rank)."""
+    import torch
+
+    events = [[(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+               for _ in parts] for _ in range(args.steps)]
+    barrier(dist)
+    torch.cuda.synchronize(device)
+    torch.cuda._sleep(int(2e6 + 3e5 * args.steps))
+    for i in range(args.steps):
+        flush.fill_(float(i))
+        for (start, end), part in zip(events[i], parts):
+            start.record(stream)
+            part()
+            end.record(stream)
+    torch.cuda.synchronize(device)
+    barrier(dist)
+    return [sum(events[i][k][0].elapsed_time(events[i][k][1]) for i in range(args.steps))
+            for k in range(len(parts))]
+
+
+def run_mixed(args, dist, world, rank, device, peaks, peak_kind):
+    """Continuous-batching step: one decode launch over the decode sequences
+    and one prefill launch over the chunks, back to back on one stream."""
+    import torch
+
+    from inferlab_b200 import workloads as wl
+
+    batch = wl.mixed_bf16(device=device, seed=2029 + rank)
+    pool = batch.pool
+    stream = torch.cuda.current_stream(device)
+    flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=f"cuda:{device}")
+    workspace = pool.make_workspace(len(batch.contexts), batch.q_heads, batch.max_context_len)
+    out_d = torch.empty_like(batch.queries)
+    out_p = torch.empty((batch.prefill_queries.shape[0], 32, 128), dtype=torch.float32,
+                        device=f"cuda:{device}")
+
+    def decode():
+        pool.decode(batch.queries, batch.block_tables, batch.context_lens, batch.max_context_len,
+                    out=out_d, workspace=workspace)
+
+    def prefill():
+        pool.prefill(batch.prefill_queries, batch.prefill_tables, batch.starts_dev,
+                     batch.counts_dev, batch.offsets_dev, int(batch.counts.max()), out=out_p)
+
+    for i in range(args.warmup):
+        flush.fill_(float(i))
+        decode()
+        prefill()
+    pool.synchronize()
+    with ClockSampler(device) as clocks:
+        ms_d, ms_p = _timed_steps(args, dist, device, stream, flush, [decode, prefill])
+    pool.synchronize()
+    step_ms = max_over_ranks(dist, (ms_d + ms_p) / args.steps)
+    dbytes = batch.decode_bytes()
+    flops = batch.prefill_flops()
+    tokens = len(batch.contexts) + int(batch.counts.sum())
+    line = {
+        "metric": "continuous-batching step ms", "value": round(step_ms, 5), "unit": "ms",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(step_ms, 5), "higher_is_better": False, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded)",
+        "config": {"workload": "32 decode seqs ctx Zipf(1.1) clip [32,8192] + 4 x 512-token "
+                               "chunked prefill, GQA 32/8 x 128 bf16, 65536-block pool",
+                   "decode_contexts": [int(c) for c in batch.contexts],
+                   "chunk_priors": [int(c) for c in batch.starts], "query_tokens": tokens},
+        "decode": {"ms": round(ms_d / args.steps, 5), "GB/s": round(dbytes / (ms_d / args.steps) / 1e6, 2),
+                   "frac_hbm": round(dbytes / (ms_d / args.steps) / 1e6 / peaks["hbm_gbs"], 4)},
+        "prefill": {"ms": round(ms_p / args.steps, 5),
+                    "TFLOP/s": round(flops / (ms_p / args.steps) / 1e9, 2),
+                    "frac_tensor": round(flops / (ms_p / args.steps) / 1e9 / peaks["bf16_tflops"], 4)},
+        "gpu_launches": 2 * args.steps, "clocks": clocks.summary(),
+    }
+    pool.close()
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if dist is not None:
+        dist.destroy_process_group()
+
+
+def run_long_sequence(args, dist, world, rank, device, peaks, peak_kind):
+    """One 131072-token sequence split across the ranks: per step, decode
+    partials over the local blocks, all-gather of (m, l, o) over NCCL, rank-order
+    log-sum-exp merge. Timed per rank with events, max over ranks."""
+    import torch
+
+    from inferlab_b200 import distributed, workloads as wl
+    from inferlab_b200.paged import lse_combine
+
+    batch = wl.long_sequence_shard(device, rank, world)
+    pool = batch.pool
+    stream = torch.cuda.current_stream(device)
+    flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=f"cuda:{device}")
+    local = int(batch.contexts[0])
+    workspace = pool.make_workspace(1, 32, local)
+
+    def step():
+        m, l, o = pool.decode_partials(batch.queries, batch.block_tables, batch.context_lens,
+                                       local, workspace=workspace)
+        if dist is not None:
+            gm, gl, go = distributed.all_gather_partials(m, l, o)
+        else:
+            gm, gl, go = m[None], l[None], o[None]
+        return lse_combine(gm, gl, go)
+
+    for i in range(args.warmup):
+        flush.fill_(float(i))
+        step()
+    pool.synchronize()
+    with ClockSampler(device) as clocks:
+        (ms,) = _timed_steps(args, dist, device, stream, flush, [step])
+    pool.synchronize()
+    total_ms = max_over_ranks(dist, ms)
+    kv_bytes = 131072 * 8 * 128 * 2 * 2
+    value = kv_bytes * args.steps / (total_ms * 1e-3) / 1e9
+    line = {
+        "metric": "long-sequence decode KV-bytes GB/s", "value": round(value, 3), "unit": "GB/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(total_ms / args.steps, 5), "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded)",
+        "config": {"workload": "one 131072-token sequence, GQA 32/8 x 128 bf16, blocks split "
+                               "across GPUs, NCCL all-gather of (m, l, o) + rank-order merge",
+                   "tokens_this_rank": local},
+        "roofline": {"bound": "hbm", "achieved_per_gpu": round(value / world, 2),
+                     "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                     "frac": round(value / world / peaks["hbm_gbs"], 4)},
+        "gpu_launches": 2 * args.steps, "clocks": clocks.summary(),
+    }
+    pool.close()
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if dist is not None:
+        dist.destroy_process_group()
+
+
 def run_reference(args):
     world, rank, _ = dist_env()
     if rank != 0:
@@ -563,7 +688,8 @@ def main():
     parser.add_argument("--warmup", type=int, default=5)
     parser.add_argument("--impl", choices=["ours", "reference"], default="ours")
     parser.add_argument("--workload", default="decode_fp32",
-                        choices=["decode_fp32", "longctx_bf16", "prefill_f16"])
+                        choices=["decode_fp32", "longctx_bf16", "prefill_f16", "mixed_bf16",
+                                 "longseq_split"])
     parser.add_argument("--cpu-seconds", type=float, default=10.0)
     parser.add_argument("--no-cpu-baseline", action="store_true")
     args = parser.parse_args()

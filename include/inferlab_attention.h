@@ -204,6 +204,28 @@ int inferlab_cuda_paged_decode(InferlabCudaKvPool* pool, const float* queries,
                                size_t error_capacity);
 
 /*
+ * One continuous-batching decode step with HOST buffers, synchronous: the
+ * per-sequence append + materialize + attention_forward loop of the
+ * reference's paged decode (worker/cpp/inferlab_runtime.cpp:2373-2393 driven
+ * by worker/src/scheduler.rs:268-270) for a whole batch in one call.
+ * queries [num_seqs][q_heads][head_dim], new_keys / new_values
+ * [num_seqs][kv_heads][head_dim] (both NULL to skip the append), block_tables
+ * [num_seqs][max_blocks_per_seq], context_lens [num_seqs] (the new token sits
+ * at position context_lens[i] - 1 and attends to [0, context_lens[i])), out
+ * [num_seqs][q_heads][head_dim]; all host memory, fp32 / int32. Inputs cross
+ * to HBM in one copy from the pool's pinned staging, then kv_append, one
+ * decode launch, one copy back; waits at most timeout_ms (0 = 10 s). Block
+ * ids and context lengths are checked on the host first (the reference's
+ * materialize checks, :776-789).
+ */
+int inferlab_cuda_decode_step_host(InferlabCudaKvPool* pool, const float* queries,
+                                   const float* new_keys, const float* new_values,
+                                   const int32_t* block_tables, uint32_t max_blocks_per_seq,
+                                   const int32_t* context_lens, uint32_t num_seqs,
+                                   uint32_t q_heads, float* out, void* stream,
+                                   uint32_t timeout_ms, char* error, size_t error_capacity);
+
+/*
  * Decode partials for a context that is split across devices: like
  * inferlab_cuda_paged_decode, but instead of the normalised output it writes,
  * per (sequence, q-head) row r = seq * q_heads + h,

@@ -1,0 +1,37 @@
+// internal.cuh - launch paths shared between the library's .cu files (not
+// part of the C ABI).
+#pragma once
+
+#include "pool.cuh"
+
+namespace ilb {
+
+// Bytes of decode workspace a batch of this shape needs, and how many of its
+// leading bytes are the split counters that must be zero before a launch.
+std::size_t decode_workspace_bytes(const InferlabCudaKvPool& pool, std::uint32_t num_seqs,
+                                   std::uint32_t q_heads, std::uint32_t max_context_len);
+std::size_t decode_counter_bytes(const InferlabCudaKvPool& pool, std::uint32_t num_seqs);
+
+// Argument checks of inferlab_cuda_paged_decode (throws std::runtime_error).
+void check_decode_arguments(const InferlabCudaKvPool& pool, const float* queries,
+                            const std::int32_t* block_tables, std::uint32_t max_blocks,
+                            const std::int32_t* context_lens, std::uint32_t num_seqs,
+                            std::uint32_t q_heads, std::uint32_t max_context_len);
+
+// Launches the decode kernel with the given workspace; the pool's device must
+// be current.
+void launch_paged_decode(InferlabCudaKvPool& pool, const float* queries,
+                         const std::int32_t* block_tables, std::uint32_t max_blocks,
+                         const std::int32_t* context_lens, std::uint32_t num_seqs,
+                         std::uint32_t q_heads, std::uint32_t max_context_len, float* out,
+                         void* workspace, std::size_t workspace_bytes, cudaStream_t stream);
+
+// Launches kv_append (see inferlab_cuda_kv_append); the pool's device must be
+// current.
+void launch_kv_append(InferlabCudaKvPool& pool, const void* key_rows, const void* value_rows,
+                      std::uint32_t row_dtype, const std::int32_t* row_sequences,
+                      const std::int32_t* positions, std::uint64_t rows,
+                      const std::int32_t* block_tables, std::uint32_t max_blocks,
+                      cudaStream_t stream);
+
+}  // namespace ilb

@@ -5,6 +5,7 @@
 // The pool's allocation policy (free list, refcounts, prefix LRU, copy on
 // write) stays on the host; only block ids cross to the device.
 #include "common.cuh"
+#include "internal.cuh"
 #include "pool.cuh"
 
 #include "../../include/inferlab_attention.h"
@@ -124,6 +125,28 @@ void launch_append(InferlabCudaKvPool& pool, const void* key_rows, const void* v
 }  // namespace
 }  // namespace ilb
 
+namespace ilb {
+
+void launch_kv_append(InferlabCudaKvPool& pool, const void* key_rows, const void* value_rows,
+                      std::uint32_t row_dtype, const std::int32_t* row_sequences,
+                      const std::int32_t* positions, std::uint64_t rows,
+                      const std::int32_t* block_tables, std::uint32_t max_blocks,
+                      cudaStream_t stream) {
+    if (pool.dtype == kFp32) {
+        launch_append<float>(pool, key_rows, value_rows, row_dtype, row_sequences, positions, rows,
+                             block_tables, max_blocks, stream);
+    } else if (pool.dtype == kF16) {
+        launch_append<__half>(pool, key_rows, value_rows, row_dtype, row_sequences, positions,
+                              rows, block_tables, max_blocks, stream);
+    } else {
+        launch_append<__nv_bfloat16>(pool, key_rows, value_rows, row_dtype, row_sequences,
+                                     positions, rows, block_tables, max_blocks, stream);
+    }
+    cuda_check(cudaGetLastError(), "kv_append launch");
+}
+
+}  // namespace ilb
+
 extern "C" int inferlab_cuda_pool_create(std::int32_t device, std::uint32_t dtype,
                                          std::uint64_t num_blocks, std::uint32_t block_tokens,
                                          std::uint32_t kv_heads, std::uint32_t head_dim,
@@ -184,6 +207,8 @@ extern "C" void inferlab_cuda_pool_destroy(InferlabCudaKvPool* pool) {
         cudaFree(pool->value_arena);
         cudaFree(pool->error_word);
         cudaFreeHost(pool->error_host);
+        if (pool->step_host != nullptr) cudaFreeHost(pool->step_host);
+        if (pool->step_device != nullptr) cudaFree(pool->step_device);
         cudaSetDevice(previous);
     }
     delete pool;

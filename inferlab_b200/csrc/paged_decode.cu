@@ -27,6 +27,7 @@
 // K/V bytes are read from HBM exactly once per (sequence, kv-head).
 #include "common.cuh"
 #include "generic_attention.cuh"
+#include "internal.cuh"
 #include "pool.cuh"
 
 #include "../../include/inferlab_attention.h"
@@ -676,6 +677,38 @@ void run_decode(InferlabCudaKvPool& p, const float* queries, const std::int32_t*
 }
 
 }  // namespace
+}  // namespace ilb
+
+// Shared launch path for decode entry points in other files (internal.cuh).
+namespace ilb {
+
+std::size_t decode_workspace_bytes(const InferlabCudaKvPool& pool, std::uint32_t num_seqs,
+                                   std::uint32_t q_heads, std::uint32_t max_context_len) {
+    const auto plan = plan_decode(num_seqs, pool.kv_heads, max_context_len);
+    return workspace_bytes_for(num_seqs, q_heads, pool.kv_heads, pool.head_dim, plan);
+}
+
+std::size_t decode_counter_bytes(const InferlabCudaKvPool& pool, std::uint32_t num_seqs) {
+    return (static_cast<std::size_t>(num_seqs) * pool.kv_heads * 4 + 255) & ~std::size_t(255);
+}
+
+void check_decode_arguments(const InferlabCudaKvPool& pool, const float* queries,
+                            const std::int32_t* block_tables, std::uint32_t max_blocks,
+                            const std::int32_t* context_lens, std::uint32_t num_seqs,
+                            std::uint32_t q_heads, std::uint32_t max_context_len) {
+    validate_decode(pool, queries, block_tables, max_blocks, context_lens, num_seqs, q_heads,
+                    max_context_len);
+}
+
+void launch_paged_decode(InferlabCudaKvPool& pool, const float* queries,
+                         const std::int32_t* block_tables, std::uint32_t max_blocks,
+                         const std::int32_t* context_lens, std::uint32_t num_seqs,
+                         std::uint32_t q_heads, std::uint32_t max_context_len, float* out,
+                         void* workspace, std::size_t workspace_bytes, cudaStream_t stream) {
+    run_decode(pool, queries, block_tables, max_blocks, context_lens, num_seqs, q_heads,
+               max_context_len, out, nullptr, nullptr, nullptr, workspace, workspace_bytes, stream);
+}
+
 }  // namespace ilb
 
 extern "C" std::size_t inferlab_cuda_paged_decode_workspace_size(const InferlabCudaKvPool* pool,

@@ -21,6 +21,11 @@ struct InferlabCudaKvPool {
     std::uint32_t* error_word = nullptr;       // device
     std::uint32_t* error_host = nullptr;       // pinned mirror
     std::mutex mutex;                          // guards error_host / error readback
+    // Grow-only staging of the host-buffer step entry (decode_step.cu).
+    std::mutex step_mutex;
+    unsigned char* step_host = nullptr;        // pinned
+    unsigned char* step_device = nullptr;
+    std::size_t step_capacity = 0;
 };
 
 namespace ilb {

@@ -215,6 +215,33 @@ class CudaKvPool:
             workspace.numel(), _stream_handle(dev, stream), error, len(error)), error)
         return out
 
+    def decode_step_host(self, queries, block_tables, context_lens, new_keys=None,
+                         new_values=None, out=None, stream=None, timeout_ms: int = 0):
+        """One synchronous decode step from host (numpy) arrays: append the new
+        token rows at context_lens - 1 (if given), decode every sequence, return
+        the output as a host array. One C call (inferlab_cuda_decode_step_host)."""
+        import numpy as np
+
+        q = np.ascontiguousarray(queries, dtype=np.float32)
+        tables = np.ascontiguousarray(block_tables, dtype=np.int32)
+        lens = np.ascontiguousarray(context_lens, dtype=np.int32)
+        num_seqs, q_heads, _ = q.shape
+        if out is None:
+            out = np.empty_like(q)
+        f32 = ctypes.POINTER(ctypes.c_float)
+        i32 = ctypes.POINTER(ctypes.c_int32)
+        keys = None if new_keys is None else np.ascontiguousarray(new_keys, dtype=np.float32)
+        values = None if new_values is None else np.ascontiguousarray(new_values, dtype=np.float32)
+        error = _lib.error_buffer()
+        _check(self._lib.inferlab_cuda_decode_step_host(
+            self._handle, q.ctypes.data_as(f32),
+            None if keys is None else keys.ctypes.data_as(f32),
+            None if values is None else values.ctypes.data_as(f32),
+            tables.ctypes.data_as(i32), tables.shape[1], lens.ctypes.data_as(i32), num_seqs,
+            q_heads, out.ctypes.data_as(f32), _stream_handle(self.device, stream), timeout_ms,
+            error, len(error)), error)
+        return out
+
     def decode_partials(self, queries: torch.Tensor, block_tables: torch.Tensor,
                         context_lens: torch.Tensor, max_context_len: int | None = None,
                         workspace: torch.Tensor | None = None, stream=None):

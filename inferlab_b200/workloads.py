@@ -207,6 +207,62 @@ def prefill_f16(device: int = 0, seed: int = 2028, num_seqs: int = 8,
                          0.5)
 
 
+def mixed_bf16(device: int = 0, seed: int = 2029, num_decode: int = 32, num_chunks: int = 4,
+               chunk_tokens: int = 512, num_blocks: int = 65536) -> PagedBatch:
+    """Continuous-batching step: num_decode decode sequences with context
+    Zipf(1.1) clipped to [32, 8192], plus num_chunks chunked-prefill segments
+    of chunk_tokens queries whose prior context is drawn from the same clipped
+    Zipf (so a chunk covers positions [prior, prior + chunk_tokens)). GQA
+    32 q / 8 kv heads x 128, bf16, one pool of num_blocks blocks with tables
+    dealt from a seeded permutation."""
+    rng = np.random.Generator(np.random.PCG64(seed))
+    contexts = zipf_contexts(rng, num_decode)
+    priors = zipf_contexts(rng, num_chunks)
+    counts = np.full(num_chunks, chunk_tokens, np.int64)
+    totals = np.concatenate([contexts, priors + counts])
+    need = (totals + BLOCK_TOKENS - 1) // BLOCK_TOKENS
+    max_blocks = int(need.max())
+    tables = _deal_tables(rng, num_blocks, need, max_blocks)
+    pool = CudaKvPool(device, KV_BF16, num_blocks, BLOCK_TOKENS, 8, 128)
+    gen = _generator(seed + 1, device)
+    _fill_arenas(pool, gen, 1.0)
+    dev = f"cuda:{device}"
+    queries = torch.randn((num_decode, 32, 128), generator=gen, device=dev, dtype=torch.float32)
+    pq = torch.randn((int(counts.sum()), 32, 128), generator=gen, device=dev,
+                     dtype=torch.float32).to(torch.bfloat16)
+    offsets = np.concatenate([[0], np.cumsum(counts)[:-1]]).astype(np.int32)
+    dt = tables[:num_decode]
+    pt = tables[num_decode:]
+    return PagedBatch(
+        pool=pool, q_heads=32, queries=queries, block_tables=torch.from_numpy(dt).to(dev),
+        context_lens=torch.from_numpy(contexts.astype(np.int32)).to(dev), contexts=contexts,
+        tables_host=dt, max_context_len=int(contexts.max()),
+        prefill_queries=pq, prefill_tables=torch.from_numpy(pt).to(dev), prefill_tables_host=pt,
+        starts=priors, counts=counts,
+        starts_dev=torch.from_numpy(priors.astype(np.int32)).to(dev),
+        counts_dev=torch.from_numpy(counts.astype(np.int32)).to(dev),
+        offsets_dev=torch.from_numpy(offsets).to(dev))
+
+
+def long_sequence_shard(device: int, rank: int, world: int, total_tokens: int = 131072,
+                        seed: int = 2030) -> PagedBatch:
+    """One total_tokens-token sequence (GQA 32/8 x 128, bf16) whose blocks are
+    split into `world` contiguous ranges; this rank's pool holds its range and
+    the batch's single decode row covers it. The query is the same on every
+    rank (seeded); K/V differ per range (seed + rank)."""
+    from .distributed import local_tokens
+
+    lo, hi = local_tokens(total_tokens, BLOCK_TOKENS, world, rank)
+    local = hi - lo
+    batch = decode_batch(device, seed + 1000 * (rank + 1), 1, np.array([local]), 32, 8, 128,
+                         KV_BF16, max_context_len=local)
+    gen = _generator(seed, device)
+    batch.queries = torch.randn((1, 32, 128), generator=gen, device=f"cuda:{device}",
+                                dtype=torch.float32)
+    batch.extra.update({"token_range": (lo, hi), "total_tokens": total_tokens})
+    return batch
+
+
 def host_arenas(pool: CudaKvPool):
     """Host copies of the arenas as numpy (fp32, or uint16 storage bits)."""
     def grab(t):
@@ -227,5 +283,5 @@ def round_queries(queries: torch.Tensor, dtype: int) -> np.ndarray:
 __all__ = [
     "PagedBatch", "decode_batch", "decode_fp32", "longctx_bf16", "longctx_contexts",
     "prefill_batch", "prefill_f16", "zipf_contexts", "host_arenas", "round_queries",
-    "KV_FP32", "KV_F16", "KV_BF16",
+    "mixed_bf16", "long_sequence_shard", "KV_FP32", "KV_F16", "KV_BF16",
 ]

@@ -132,6 +132,44 @@ def test_partials_and_combine_equal_whole_context(torch_mod, wl, oracle_mod):
     batch.pool.close()
 
 
+def test_decode_step_host_matches_device_calls(torch_mod, wl, oracle_mod):
+    """inferlab_cuda_decode_step_host (host buffers, append + decode in one
+    call) equals kv_append followed by paged decode, and the oracle."""
+    torch = torch_mod
+    contexts = np.array([1, 16, 17, 700, 2048, 33])
+    batch = wl.decode_batch(0, 17, len(contexts), contexts, 32, 8, 128, wl.KV_BF16,
+                            max_context_len=2048)
+    rng = np.random.Generator(np.random.PCG64(18))
+    q = rng.standard_normal((len(contexts), 32, 128), dtype=np.float32)
+    k_new = rng.standard_normal((len(contexts), 8, 128), dtype=np.float32)
+    v_new = rng.standard_normal((len(contexts), 8, 128), dtype=np.float32)
+    for repeat in range(2):  # the second call reuses the pool's staging
+        got = batch.pool.decode_step_host(q, batch.tables_host, contexts, k_new, v_new)
+    dev = "cuda:0"
+    ref = batch.pool.decode(torch.from_numpy(q).to(dev), batch.block_tables, batch.context_lens,
+                            2048)
+    batch.pool.synchronize()
+    close(got, ref.cpu().numpy())
+    k_host, v_host = wl.host_arenas(batch.pool)
+    ref_o = oracle_mod.paged_attention(k_host, v_host, wl.KV_BF16, batch.tables_host,
+                                       contexts - 1, np.ones(len(contexts)),
+                                       wl.round_queries(torch.from_numpy(q), wl.KV_BF16), 32)
+    close(got, ref_o)
+    # the appended rows are in the pool at position ctx - 1
+    kg, _ = batch.pool.gather(batch.block_tables[4, :128].contiguous(), 2048)
+    assert torch.equal(kg[2047].cpu(), torch.from_numpy(k_new[4]).to(torch.bfloat16))
+    # host-side checks fire before any device work
+    from inferlab_b200 import AttentionError
+
+    bad = batch.tables_host.copy()
+    bad[2, 1] = -3
+    with pytest.raises(AttentionError, match="^paged KV block table contains an invalid page$"):
+        batch.pool.decode_step_host(q, bad, contexts)
+    with pytest.raises(AttentionError, match="^paged KV context length is invalid$"):
+        batch.pool.decode_step_host(q, batch.tables_host, contexts * 0)
+    batch.pool.close()
+
+
 def test_append_then_gather_bit_exact(torch_mod, wl, oracle_mod):
     torch = torch_mod
     from inferlab_b200 import CudaKvPool
