@@ -204,6 +204,25 @@ int inferlab_cuda_paged_decode(InferlabCudaKvPool* pool, const float* queries,
                                size_t error_capacity);
 
 /*
+ * inferlab_cuda_paged_decode without a caller workspace, for callers that
+ * cannot allocate device memory (for example a process whose GPU memory is
+ * reserved up front by another framework's allocator, or a serving loop that
+ * may not call cudaMalloc once running). No counterpart in the reference,
+ * whose decode runs on the host. The split-KV scratch is a 16 MiB array built
+ * into the library (held by every GPU that loads it until the process exits);
+ * batches needing more scratch than that are rejected with an error naming
+ * the size. The call allocates nothing. Calls share the array: two calls whose
+ * work overlaps on the GPU race, so serialise them. The first call on a device
+ * looks up the array's device address; make it before any stream capture.
+ * Arguments as inferlab_cuda_paged_decode.
+ */
+int inferlab_cuda_paged_decode_noalloc(InferlabCudaKvPool* pool, const float* queries,
+                                       const int32_t* block_tables, uint32_t max_blocks_per_seq,
+                                       const int32_t* context_lens, uint32_t num_seqs,
+                                       uint32_t q_heads, uint32_t max_context_len, float* out,
+                                       void* stream, char* error, size_t error_capacity);
+
+/*
  * One continuous-batching decode step with HOST buffers, synchronous: the
  * per-sequence append + materialize + attention_forward loop of the
  * reference's paged decode (worker/cpp/inferlab_runtime.cpp:2373-2393 driven
