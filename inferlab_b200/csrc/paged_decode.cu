@@ -43,6 +43,7 @@ constexpr int kDecodeBlockTokens = 16;
 constexpr int kDecodeWarps = 4;
 constexpr int kDecodeStages = 2;
 constexpr int kMaxBlocksPerSplit = 256;
+constexpr std::uint32_t kMaxSplits = 512;
 
 template <typename KvT, int D, int GROUP>
 struct DecodeShape {
@@ -100,6 +101,7 @@ struct DecodeSmem {
     static constexpr std::size_t kRedMl = kRedAcc + static_cast<std::size_t>(kDecodeWarps) * GROUP * D * 4;
     static constexpr std::size_t kFlag = kRedMl + kDecodeWarps * GROUP * 2 * 4;
     static constexpr std::size_t kBytes = kFlag + 16;
+    static_assert(GROUP * kMaxSplits * 4 <= kTilesBytes, "split weights must fit the tile area");
 };
 
 __device__ __forceinline__ float safe_max(float m) { return m == -INFINITY ? 0.0f : m; }
@@ -408,22 +410,48 @@ __global__ void __launch_bounds__(kDecodeWarps * 32)
     __syncthreads();
     if (*flag != 2) return;
     __threadfence();
+    // Split weights, once per q-head (one warp per head), into the tile area,
+    // which no copy uses any more: w[h][sp] = 2^(m_sp - M_h), and per head
+    // (M_h, L_h = sum_sp l_sp w[h][sp]) into red_ml.
+    float* w = reinterpret_cast<float*>(smem);
+    for (int h = warp; h < GROUP; h += kDecodeWarps) {
+        const float* ml = p.ws_ml + (row0 + h) * p.max_splits * 2;
+        float mw = -INFINITY;
+        for (int sp = lane; sp < nsplit; sp += 32) mw = fmaxf(mw, __ldcg(ml + sp * 2));
+        mw = warp_max(mw);
+        const float base = safe_max(mw);
+        float lsum = 0.0f;
+        for (int sp = lane; sp < nsplit; sp += 32) {
+            const float f = exp2f(__ldcg(ml + sp * 2) - base);
+            w[h * nsplit + sp] = f;
+            lsum += __ldcg(ml + sp * 2 + 1) * f;
+        }
+        lsum = warp_sum(lsum);
+        if (lane == 0) {
+            red_ml[h * 2] = mw;
+            red_ml[h * 2 + 1] = lsum;
+        }
+    }
+    __syncthreads();
     for (int i = threadIdx.x; i < GROUP * D; i += blockDim.x) {
         const int h = i / D;
         const int dim = i % D;
         const std::size_t row = row0 + h;
-        const float* ml = p.ws_ml + row * p.max_splits * 2;
         const float* o = p.ws_o + row * p.max_splits * D + dim;
-        float mw = -INFINITY;
-        for (int sp = 0; sp < nsplit; ++sp) mw = fmaxf(mw, __ldcg(ml + sp * 2));
-        const float base = safe_max(mw);
-        float lsum = 0.0f;
-        float a = 0.0f;
-        for (int sp = 0; sp < nsplit; ++sp) {
-            const float f = exp2f(__ldcg(ml + sp * 2) - base);
-            lsum += __ldcg(ml + sp * 2 + 1) * f;
-            a += __ldcg(o + static_cast<std::size_t>(sp) * D) * f;
+        const float* wh = w + h * nsplit;
+        // Four independent sums so the L2 loads of consecutive splits overlap.
+        float a0 = 0.0f, a1 = 0.0f, a2 = 0.0f, a3 = 0.0f;
+        int sp = 0;
+        for (; sp + 4 <= nsplit; sp += 4) {
+            a0 = fmaf(__ldcg(o + static_cast<std::size_t>(sp) * D), wh[sp], a0);
+            a1 = fmaf(__ldcg(o + static_cast<std::size_t>(sp + 1) * D), wh[sp + 1], a1);
+            a2 = fmaf(__ldcg(o + static_cast<std::size_t>(sp + 2) * D), wh[sp + 2], a2);
+            a3 = fmaf(__ldcg(o + static_cast<std::size_t>(sp + 3) * D), wh[sp + 3], a3);
         }
+        for (; sp < nsplit; ++sp) a0 = fmaf(__ldcg(o + static_cast<std::size_t>(sp) * D), wh[sp], a0);
+        const float a = (a0 + a1) + (a2 + a3);
+        const float mw = red_ml[h * 2];
+        const float lsum = red_ml[h * 2 + 1];
         if (p.emit_partials) {
             p.part_o[row * D + dim] = a;
             if (dim == 0) {
@@ -489,7 +517,13 @@ DecodePlan plan_decode(std::uint32_t num_seqs, std::uint32_t kv_heads,
         bps = static_cast<std::uint32_t>((max_blocks + splits - 1) / splits);
         bps = std::max<std::uint32_t>(bps, 8);
     }
-    bps = std::min<std::uint32_t>(std::max<std::uint32_t>(bps, 1), kMaxBlocksPerSplit);
+    bps = std::max<std::uint32_t>(bps, 1);
+    // The fused merge keeps one weight per (q-head, split) in the tile area:
+    // at most kMaxSplits splits per context.
+    bps = std::max<std::uint32_t>(bps, (max_blocks + kMaxSplits - 1) / kMaxSplits);
+    if (bps > kMaxBlocksPerSplit) {
+        throw std::runtime_error("paged decode context is longer than the kernel supports (2097152 tokens)");
+    }
     const std::uint32_t max_splits = std::max<std::uint32_t>(1, (max_blocks + bps - 1) / bps);
     return DecodePlan{bps, max_splits};
 }
@@ -716,8 +750,12 @@ extern "C" std::size_t inferlab_cuda_paged_decode_workspace_size(const InferlabC
                                                                  std::uint32_t q_heads,
                                                                  std::uint32_t max_context_len) {
     if (pool == nullptr || num_seqs == 0 || q_heads == 0 || max_context_len == 0) return 0;
-    const auto plan = ilb::plan_decode(num_seqs, pool->kv_heads, max_context_len);
-    return ilb::workspace_bytes_for(num_seqs, q_heads, pool->kv_heads, pool->head_dim, plan);
+    try {
+        const auto plan = ilb::plan_decode(num_seqs, pool->kv_heads, max_context_len);
+        return ilb::workspace_bytes_for(num_seqs, q_heads, pool->kv_heads, pool->head_dim, plan);
+    } catch (...) {
+        return 0;  // the decode call itself reports why
+    }
 }
 
 extern "C" int inferlab_cuda_paged_decode_workspace_init(void* workspace,
