@@ -517,7 +517,7 @@ DecodePlan plan_decode(std::uint32_t num_seqs, std::uint32_t kv_heads,
         bps = static_cast<std::uint32_t>((max_blocks + splits - 1) / splits);
         bps = std::max<std::uint32_t>(bps, 8);
     }
-    bps = std::max<std::uint32_t>(bps, 1);
+    bps = std::min<std::uint32_t>(std::max<std::uint32_t>(bps, 1), kMaxBlocksPerSplit);
     // The fused merge keeps one weight per (q-head, split) in the tile area:
     // at most kMaxSplits splits per context.
     bps = std::max<std::uint32_t>(bps, (max_blocks + kMaxSplits - 1) / kMaxSplits);
