@@ -259,6 +259,45 @@ __device__ __forceinline__ void bulk_copy_g2s(void* dst, const void* src, std::u
         : "memory");
 }
 
+// Packed fp32 pairs (sm_100 f32x2 arithmetic: one instruction for two lanes
+// of work) and the hardware base-2 exponential (ex2.approx, flush to zero).
+__device__ __forceinline__ std::uint64_t pack_f32x2(float lo, float hi) {
+    std::uint64_t r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+    return r;
+}
+__device__ __forceinline__ std::uint64_t pack_u32x2(std::uint32_t lo, std::uint32_t hi) {
+    std::uint64_t r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "r"(lo), "r"(hi));
+    return r;
+}
+__device__ __forceinline__ float low_f32(std::uint64_t v) {
+    float lo, hi;
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+    return lo;
+}
+__device__ __forceinline__ float high_f32(std::uint64_t v) {
+    float lo, hi;
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+    return hi;
+}
+__device__ __forceinline__ std::uint64_t ffma_f32x2(std::uint64_t a, std::uint64_t b,
+                                                    std::uint64_t c) {
+    std::uint64_t d;
+    asm("fma.rn.ftz.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+    return d;
+}
+__device__ __forceinline__ std::uint64_t fadd_f32x2(std::uint64_t a, std::uint64_t b) {
+    std::uint64_t d;
+    asm("add.rn.ftz.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+__device__ __forceinline__ float ex2_ftz(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
 __device__ __forceinline__ float warp_max(float v) {
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, off));

@@ -42,8 +42,10 @@ namespace {
 constexpr int kDecodeBlockTokens = 16;
 constexpr int kDecodeWarps = 4;
 constexpr int kDecodeStages = 2;
-constexpr int kMaxBlocksPerSplit = 256;
-constexpr std::uint32_t kMaxSplits = 512;
+constexpr int kMaxBlocksPerSplit = 1024;
+// Splits per context are capped so that the last CTA's merge stays short
+// (at 64 splits it reads 64 x (head_dim + 2) floats per q-head).
+constexpr std::uint32_t kMaxSplits = 64;
 
 template <typename KvT, int D, int GROUP>
 struct DecodeShape {
@@ -433,34 +435,49 @@ __global__ void __launch_bounds__(kDecodeWarps * 32)
         }
     }
     __syncthreads();
-    for (int i = threadIdx.x; i < GROUP * D; i += blockDim.x) {
-        const int h = i / D;
-        const int dim = i % D;
+    // Each thread merges four consecutive dims (one float4 per split), eight
+    // splits in flight at a time, so the L2 reads of the partials overlap.
+    for (int i4 = threadIdx.x; i4 < GROUP * D / 4; i4 += blockDim.x) {
+        const int h = (i4 * 4) / D;
+        const int dim = (i4 * 4) % D;
         const std::size_t row = row0 + h;
-        const float* o = p.ws_o + row * p.max_splits * D + dim;
+        const float4* o = reinterpret_cast<const float4*>(p.ws_o + row * p.max_splits * D + dim);
         const float* wh = w + h * nsplit;
-        // Four independent sums so the L2 loads of consecutive splits overlap.
-        float a0 = 0.0f, a1 = 0.0f, a2 = 0.0f, a3 = 0.0f;
+        float4 a = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
         int sp = 0;
-        for (; sp + 4 <= nsplit; sp += 4) {
-            a0 = fmaf(__ldcg(o + static_cast<std::size_t>(sp) * D), wh[sp], a0);
-            a1 = fmaf(__ldcg(o + static_cast<std::size_t>(sp + 1) * D), wh[sp + 1], a1);
-            a2 = fmaf(__ldcg(o + static_cast<std::size_t>(sp + 2) * D), wh[sp + 2], a2);
-            a3 = fmaf(__ldcg(o + static_cast<std::size_t>(sp + 3) * D), wh[sp + 3], a3);
+        for (; sp + 8 <= nsplit; sp += 8) {
+            float4 x[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u) x[u] = __ldcg(o + static_cast<std::size_t>(sp + u) * (D / 4));
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+                const float f = wh[sp + u];
+                a.x = fmaf(x[u].x, f, a.x);
+                a.y = fmaf(x[u].y, f, a.y);
+                a.z = fmaf(x[u].z, f, a.z);
+                a.w = fmaf(x[u].w, f, a.w);
+            }
         }
-        for (; sp < nsplit; ++sp) a0 = fmaf(__ldcg(o + static_cast<std::size_t>(sp) * D), wh[sp], a0);
-        const float a = (a0 + a1) + (a2 + a3);
+        for (; sp < nsplit; ++sp) {
+            const float4 x = __ldcg(o + static_cast<std::size_t>(sp) * (D / 4));
+            const float f = wh[sp];
+            a.x = fmaf(x.x, f, a.x);
+            a.y = fmaf(x.y, f, a.y);
+            a.z = fmaf(x.z, f, a.z);
+            a.w = fmaf(x.w, f, a.w);
+        }
         const float mw = red_ml[h * 2];
         const float lsum = red_ml[h * 2 + 1];
         if (p.emit_partials) {
-            p.part_o[row * D + dim] = a;
+            *reinterpret_cast<float4*>(p.part_o + row * D + dim) = a;
             if (dim == 0) {
                 p.part_m[row] = mw * kLn2;
                 p.part_l[row] = lsum;
             }
         } else {
             if (dim == 0 && !(isfinite(lsum) && lsum > 0.0f)) flag_error(p.error_word, kErrNormalizer);
-            p.out[row * D + dim] = a / lsum;
+            *reinterpret_cast<float4*>(p.out + row * D + dim) =
+                make_float4(a.x / lsum, a.y / lsum, a.z / lsum, a.w / lsum);
         }
     }
     if (threadIdx.x == 0) p.ws_count[pair] = 0;
@@ -522,7 +539,8 @@ DecodePlan plan_decode(std::uint32_t num_seqs, std::uint32_t kv_heads,
     // at most kMaxSplits splits per context.
     bps = std::max<std::uint32_t>(bps, (max_blocks + kMaxSplits - 1) / kMaxSplits);
     if (bps > kMaxBlocksPerSplit) {
-        throw std::runtime_error("paged decode context is longer than the kernel supports (2097152 tokens)");
+        throw std::runtime_error(
+            "paged decode context is longer than the kernel supports (1048576 tokens)");
     }
     const std::uint32_t max_splits = std::max<std::uint32_t>(1, (max_blocks + bps - 1) / bps);
     return DecodePlan{bps, max_splits};

@@ -1,28 +1,38 @@
 // prefill_tc.cuh - causal / chunked prefill on the sm_100a tensor cores.
 //
-// Work item: one CTA per (segment, q-head, 128-query tile). The keys a query
-// may see follow legal_sources (kernels/attention_cpu.cpp:113-123): query i of
-// a segment starting at position P sees keys [0, P + i].
+// Work item: one CTA per (segment, q-head, 256-query block) = two 128-query
+// tiles A and B that share every K/V tile. The keys a query may see follow
+// legal_sources (kernels/attention_cpu.cpp:113-123): query i of a segment that
+// starts at position P sees keys [0, P + i].
 //
-// Roles (192 threads):
-//   warps 0-3  softmax: thread t owns query row t. S rows come out of TMEM with
-//              tcgen05.ld (32x32b: one lane per row, no shuffles), the running
-//              max / sum are per thread, P is written to shared memory as
-//              fp16 in the 128-byte-swizzled K-major layout the MMA reads, and
-//              O lives in 128 fp32 registers per thread.
-//   warp 4     TMA producer: Q tile once (3-D map over [tokens][q_heads][128]),
-//              then per 128-key tile eight 16-token blocks of K and of V, each
-//              a box of the 4-D map over the arena [block][kv_head][slot][128]
-//              at the block id the table names (no multicast).
-//   warp 5     MMA issuer: S = Q K^T (M=N=128, K=128, f16/bf16 in, fp32 out)
-//              into one of two TMEM buffers, so S(j+1) runs while softmax(j)
-//              works; PV(j) = P_j V_j (V as an MN-major operand) into a third
-//              TMEM buffer, which softmax(j+1) folds into O after rescaling:
-//              O <- (O + PV(j)) * alpha(j+1), the online-softmax recurrence of
-//              kernels/attention_cpu.cpp:364-386 in the log2 domain.
+// Roles (352 threads):
+//   warps 0-3 / 4-7  softmax for tile A / B: thread t owns query row t. Per
+//              128-key tile it reads its S row from TMEM once (tcgen05.ld
+//              32x32b.x128), masks, takes the row max, computes fp16
+//              probabilities and writes them back into TMEM over the first 64
+//              columns of S (tcgen05.st), where the PV MMA reads them as its A
+//              operand. O stays in TMEM, accumulated by the MMA; it is rescaled
+//              (load, multiply, store in TMEM) only when a row's running max
+//              grows by more than 2^8, so probabilities relative to the kept
+//              max stay <= 256 (exact in fp16's range) and the result is the
+//              same online-softmax recurrence (kernels/attention_cpu.cpp:364-386).
+//   warp 8     TMA producer: both Q tiles once (3-D map over
+//              [tokens][q_heads][128]), then per 128-key tile eight 16-token
+//              blocks of K and of V, each a box of the 4-D map over the arena
+//              [block][kv_head][slot][128] at the block id the table names
+//              (no multicast).
+//   warp 9     MMA issuer: S_t = Q_t K^T (M=N=128, K=128, f16/bf16, fp32 in
+//              TMEM) for both tiles, then O_t += P_t V (P from TMEM, V an
+//              MN-major shared-memory operand), so the tensor core works on one
+//              tile while the other tile's softmax runs.
+//   warp 10    (bf16 pools) widens each V tile from bf16 to fp16 in shared
+//              memory before its PV, so P keeps fp16's 11-bit significand.
+// TMEM (512 columns): tile t uses [256t, 256t + 128) for S / P and
+// [256t + 128, 256t + 256) for O.
 // Every mbarrier wait is bounded; a wait that gives up records
-// kErrWaitTimeout, the CTA drains its own copies and MMAs (bounded) and frees
-// its TMEM before returning.
+// kErrWaitTimeout, and the CTA drains its own copies and MMAs (bounded) and
+// frees its TMEM before returning. Warp-collective TMEM instructions are only
+// ever reached by whole warps.
 #pragma once
 
 #include <cuda.h>
@@ -37,34 +47,35 @@
 namespace ilb {
 namespace tc {
 
-constexpr int kBM = 128;
-constexpr int kBN = 128;
+constexpr int kBM = 128;                 // rows of one Q tile
+constexpr int kQBlock = 2 * kBM;         // queries per CTA (tiles A and B)
+constexpr int kBN = 128;                 // keys per K/V tile
 constexpr int kD = 128;
 constexpr int kBlockTokens = 16;
-constexpr int kThreads = 192;
+constexpr int kThreads = 352;
 constexpr int kHalf = 16384;             // one 64-column half of a 128 x 128 16-bit tile
 constexpr int kTile = 2 * kHalf;         // 32 KB
-constexpr int kQ = 0;
-constexpr int kK0 = kQ + kTile;          // two K stages
+constexpr int kQ0 = 0;                   // Q tiles A, B
+constexpr int kK0 = 2 * kTile;           // two K stages
 constexpr int kV0 = kK0 + 2 * kTile;     // two V stages
-constexpr int kP = kV0 + 2 * kTile;
-constexpr int kBars = kP + kTile;        // 192 KB
-constexpr int kNumBars = 16;
+constexpr int kBars = kV0 + 2 * kTile;   // 192 KB
+constexpr int kNumBars = 20;
 constexpr int kSmemBytes = kBars + kNumBars * 8 + 64;
 constexpr int kSmemAlloc = kSmemBytes + 1024;  // slack to align the base to 1024 B
-constexpr uint32_t kTmemCols = 512;      // S0 [0,128) S1 [128,256) PV [256,384)
+constexpr uint32_t kTmemCols = 512;
+constexpr float kRescaleThreshold = 8.0f;  // log2 units: rescale O when the max grows by > 2^8
 
 enum Bar : int {
     kBarQ = 0,
-    kBarK = 1,      // +stage
-    kBarV = 3,      // +stage
-    kBarS = 5,      // +buffer
-    kBarSFree = 7,  // +buffer, 128 arrivals
-    kBarP = 9,      // 128 arrivals
-    kBarPV = 10,
-    kBarKFree = 11, // +stage
-    kBarVFree = 13, // +stage
-    kBarDone = 15,
+    kBarK = 1,       // +stage
+    kBarV = 3,       // +stage
+    kBarKFree = 5,   // +stage
+    kBarVFree = 7,   // +stage
+    kBarS = 9,       // +tile
+    kBarP = 11,      // +tile, 128 arrivals
+    kBarO = 13,      // +tile
+    kBarVReady = 15, // +stage, 32 arrivals (bf16 widening)
+    kBarDone = 17,
 };
 
 struct Params {
@@ -76,7 +87,7 @@ struct Params {
     std::uint32_t num_segments;
     std::uint32_t q_heads;
     std::uint32_t group;
-    std::uint32_t q_tiles;
+    std::uint32_t q_blocks;
     std::uint64_t num_blocks;
     long long total_queries;
     float scale_log2;
@@ -167,6 +178,52 @@ __device__ __forceinline__ void tmem_load32(std::uint32_t taddr, float* out) {
     for (int i = 0; i < 32; ++i) out[i] = __uint_as_float(r[i]);
 }
 
+// O (+)= P V with P read from TMEM (the A operand, K-major: row r at lane r,
+// 16-bit elements packed two per 32-bit column) and V from shared memory.
+__device__ __forceinline__ void mma_f16_tmem_a(std::uint32_t d_tmem, std::uint32_t a_tmem,
+                                               std::uint64_t b_desc, std::uint32_t idesc,
+                                               std::uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+// 128 consecutive TMEM columns of this thread's lane (32x32b.x128) in one
+// load; the wait names every destination register so no use can be scheduled
+// before the data has landed.
+__device__ __forceinline__ void tmem_load128(std::uint32_t taddr, std::uint32_t* r) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x128.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32, %33, %34, %35, %36, %37, %38, %39, %40, %41, %42, %43, %44, %45, %46, %47, %48, %49, %50, %51, %52, %53, %54, %55, %56, %57, %58, %59, %60, %61, %62, %63, %64, %65, %66, %67, %68, %69, %70, %71, %72, %73, %74, %75, %76, %77, %78, %79, %80, %81, %82, %83, %84, %85, %86, %87, %88, %89, %90, %91, %92, %93, %94, %95, %96, %97, %98, %99, %100, %101, %102, %103, %104, %105, %106, %107, %108, %109, %110, %111, %112, %113, %114, %115, %116, %117, %118, %119, %120, %121, %122, %123, %124, %125, %126, %127}, [%128];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31]), "=r"(r[32]), "=r"(r[33]), "=r"(r[34]), "=r"(r[35]), "=r"(r[36]), "=r"(r[37]), "=r"(r[38]), "=r"(r[39]), "=r"(r[40]), "=r"(r[41]), "=r"(r[42]), "=r"(r[43]), "=r"(r[44]), "=r"(r[45]), "=r"(r[46]), "=r"(r[47]), "=r"(r[48]), "=r"(r[49]), "=r"(r[50]), "=r"(r[51]), "=r"(r[52]), "=r"(r[53]), "=r"(r[54]), "=r"(r[55]), "=r"(r[56]), "=r"(r[57]), "=r"(r[58]), "=r"(r[59]), "=r"(r[60]), "=r"(r[61]), "=r"(r[62]), "=r"(r[63]), "=r"(r[64]), "=r"(r[65]), "=r"(r[66]), "=r"(r[67]), "=r"(r[68]), "=r"(r[69]), "=r"(r[70]), "=r"(r[71]), "=r"(r[72]), "=r"(r[73]), "=r"(r[74]), "=r"(r[75]), "=r"(r[76]), "=r"(r[77]), "=r"(r[78]), "=r"(r[79]), "=r"(r[80]), "=r"(r[81]), "=r"(r[82]), "=r"(r[83]), "=r"(r[84]), "=r"(r[85]), "=r"(r[86]), "=r"(r[87]), "=r"(r[88]), "=r"(r[89]), "=r"(r[90]), "=r"(r[91]), "=r"(r[92]), "=r"(r[93]), "=r"(r[94]), "=r"(r[95]), "=r"(r[96]), "=r"(r[97]), "=r"(r[98]), "=r"(r[99]), "=r"(r[100]), "=r"(r[101]), "=r"(r[102]), "=r"(r[103]), "=r"(r[104]), "=r"(r[105]), "=r"(r[106]), "=r"(r[107]), "=r"(r[108]), "=r"(r[109]), "=r"(r[110]), "=r"(r[111]), "=r"(r[112]), "=r"(r[113]), "=r"(r[114]), "=r"(r[115]), "=r"(r[116]), "=r"(r[117]), "=r"(r[118]), "=r"(r[119]), "=r"(r[120]), "=r"(r[121]), "=r"(r[122]), "=r"(r[123]), "=r"(r[124]), "=r"(r[125]), "=r"(r[126]), "=r"(r[127])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]), "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]), "+r"(r[15]), "+r"(r[16]), "+r"(r[17]), "+r"(r[18]), "+r"(r[19]), "+r"(r[20]), "+r"(r[21]), "+r"(r[22]), "+r"(r[23]), "+r"(r[24]), "+r"(r[25]), "+r"(r[26]), "+r"(r[27]), "+r"(r[28]), "+r"(r[29]), "+r"(r[30]), "+r"(r[31]), "+r"(r[32]), "+r"(r[33]), "+r"(r[34]), "+r"(r[35]), "+r"(r[36]), "+r"(r[37]), "+r"(r[38]), "+r"(r[39]), "+r"(r[40]), "+r"(r[41]), "+r"(r[42]), "+r"(r[43]), "+r"(r[44]), "+r"(r[45]), "+r"(r[46]), "+r"(r[47]), "+r"(r[48]), "+r"(r[49]), "+r"(r[50]), "+r"(r[51]), "+r"(r[52]), "+r"(r[53]), "+r"(r[54]), "+r"(r[55]), "+r"(r[56]), "+r"(r[57]), "+r"(r[58]), "+r"(r[59]), "+r"(r[60]), "+r"(r[61]), "+r"(r[62]), "+r"(r[63]), "+r"(r[64]), "+r"(r[65]), "+r"(r[66]), "+r"(r[67]), "+r"(r[68]), "+r"(r[69]), "+r"(r[70]), "+r"(r[71]), "+r"(r[72]), "+r"(r[73]), "+r"(r[74]), "+r"(r[75]), "+r"(r[76]), "+r"(r[77]), "+r"(r[78]), "+r"(r[79]), "+r"(r[80]), "+r"(r[81]), "+r"(r[82]), "+r"(r[83]), "+r"(r[84]), "+r"(r[85]), "+r"(r[86]), "+r"(r[87]), "+r"(r[88]), "+r"(r[89]), "+r"(r[90]), "+r"(r[91]), "+r"(r[92]), "+r"(r[93]), "+r"(r[94]), "+r"(r[95]), "+r"(r[96]), "+r"(r[97]), "+r"(r[98]), "+r"(r[99]), "+r"(r[100]), "+r"(r[101]), "+r"(r[102]), "+r"(r[103]), "+r"(r[104]), "+r"(r[105]), "+r"(r[106]), "+r"(r[107]), "+r"(r[108]), "+r"(r[109]), "+r"(r[110]), "+r"(r[111]), "+r"(r[112]), "+r"(r[113]), "+r"(r[114]), "+r"(r[115]), "+r"(r[116]), "+r"(r[117]), "+r"(r[118]), "+r"(r[119]), "+r"(r[120]), "+r"(r[121]), "+r"(r[122]), "+r"(r[123]), "+r"(r[124]), "+r"(r[125]), "+r"(r[126]), "+r"(r[127]) : : "memory");
+}
+
+// Stores 32 registers into 32 consecutive TMEM columns of this thread's lane.
+__device__ __forceinline__ void tmem_store32(std::uint32_t taddr, const std::uint32_t* r) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};"
+        :
+        : "r"(taddr), "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+        : "memory");
+}
+
+// Stores 16 registers into 16 consecutive TMEM columns of this thread's lane.
+__device__ __forceinline__ void tmem_store16(std::uint32_t taddr, const std::uint32_t* r) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16};"
+        :
+        : "r"(taddr), "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+        : "memory");
+}
+
+__device__ __forceinline__ void tmem_store_wait() {
+    asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+
 // Shared-memory matrix descriptor (sm_100 layout): start, leading and stride
 // byte offsets in 16-byte units, version 1, 128-byte swizzle.
 __device__ __forceinline__ std::uint64_t sw128_desc(std::uint32_t saddr, std::uint32_t lbo,
@@ -215,37 +272,45 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
 
-    // Work item, heaviest (last) query tiles first.
-    const std::uint32_t tile = p.q_tiles - 1 - blockIdx.x % p.q_tiles;
-    const std::uint32_t head = (blockIdx.x / p.q_tiles) % p.q_heads;
-    const std::uint32_t seg = blockIdx.x / (p.q_tiles * p.q_heads);
+    // Work item, heaviest (last) query blocks first.
+    const std::uint32_t qblk = p.q_blocks - 1 - blockIdx.x % p.q_blocks;
+    const std::uint32_t head = (blockIdx.x / p.q_blocks) % p.q_heads;
+    const std::uint32_t seg = blockIdx.x / (p.q_blocks * p.q_heads);
     const int count = p.counts[seg];
-    const int q_lo = static_cast<int>(tile) * kBM;
+    const int q_lo = static_cast<int>(qblk) * kQBlock;
     if (q_lo >= count) return;
     const int start = p.starts[seg];
     const int offset = p.offsets[seg];
-    const int total = start + count;
     if (start < 0 || count < 1 || offset < 0 ||
         static_cast<long long>(offset) + count > p.total_queries ||
         static_cast<long long>(start) + count > static_cast<long long>(p.max_blocks) * kBlockTokens) {
         if (threadIdx.x == 0) flag_error(p.error_word, kErrSegment);
         return;
     }
-    const int rows = min(kBM, count - q_lo);
-    const int kv_end = start + q_lo + rows;  // keys [0, kv_end) are visible to this tile
-    const int n_tiles = (kv_end + kBN - 1) / kBN;
-    const int nblk_total = (total + kBlockTokens - 1) / kBlockTokens;
+    // Per tile: rows inside the segment and how many K/V tiles it needs.
+    int rows[2];
+    int ntiles[2];
+#pragma unroll
+    for (int t = 0; t < 2; ++t) {
+        rows[t] = max(0, min(kBM, count - (q_lo + t * kBM)));
+        ntiles[t] = rows[t] > 0 ? (start + q_lo + t * kBM + rows[t] + kBN - 1) / kBN : 0;
+    }
+    const int n_total = max(ntiles[0], ntiles[1]);
+    const int nblk_total = (start + count + kBlockTokens - 1) / kBlockTokens;
     const std::uint32_t kv_head = head / p.group;
     const std::int32_t* table = p.tables + static_cast<std::size_t>(seg) * p.max_blocks;
 
     if (threadIdx.x == 0) {
         for (int b = 0; b < kNumBars; ++b) {
-            mbar_init(&bars[b], (b == kBarSFree || b == kBarSFree + 1 || b == kBarP) ? 128 : 1);
+            std::uint32_t arrivals = 1;
+            if (b == kBarP || b == kBarP + 1) arrivals = 128;
+            if (b == kBarVReady || b == kBarVReady + 1) arrivals = 32;
+            mbar_init(&bars[b], arrivals);
         }
         *abort = 0;
         fence_barrier_init();
     }
-    if (warp == 5) {
+    if (warp == 9) {
         tmem_alloc(tmem_slot, kTmemCols);
         tmem_relinquish();
     }
@@ -255,15 +320,19 @@ __global__ void __launch_bounds__(kThreads, 1)
     const std::uint32_t tmem = *tmem_slot;
     const Waiter wait{abort, p.error_word};
 
-    if (warp == 4) {
+    if (warp == 8) {
         // ------------------------------------------------------------ producer
         if (lane == 0) {
-            mbar_arrive_expect_tx(&bars[kBarQ], kTile);
-            tma_load_3d(smem + kQ, &q_map, 0, static_cast<int>(head), offset + q_lo, &bars[kBarQ]);
-            tma_load_3d(smem + kQ + kHalf, &q_map, 64, static_cast<int>(head), offset + q_lo,
-                        &bars[kBarQ]);
+            mbar_arrive_expect_tx(&bars[kBarQ], 2 * kTile);
+#pragma unroll
+            for (int t = 0; t < 2; ++t) {
+                tma_load_3d(smem + kQ0 + t * kTile, &q_map, 0, static_cast<int>(head),
+                            offset + q_lo + t * kBM, &bars[kBarQ]);
+                tma_load_3d(smem + kQ0 + t * kTile + kHalf, &q_map, 64, static_cast<int>(head),
+                            offset + q_lo + t * kBM, &bars[kBarQ]);
+            }
             int issued = 0;
-            for (int j = 0; j < n_tiles; ++j) {
+            for (int j = 0; j < n_total; ++j) {
                 const int st = j & 1;
                 if (j >= 2 && !wait(&bars[kBarKFree + st], ((j >> 1) - 1) & 1)) break;
                 std::int32_t ids[8];
@@ -309,175 +378,190 @@ __global__ void __launch_bounds__(kThreads, 1)
                 mbar_wait_bounded(&bars[bar], (j >> 1) & 1, p.error_word);
             }
         }
-    } else if (warp == 5) {
+    } else if (warp == 9) {
         // ------------------------------------------------------------ MMA issuer
         if (lane == 0) {
-            constexpr std::uint32_t a_type = kBf16 ? 1u : 0u;
-            const std::uint32_t idesc_s = idesc_f16(a_type, a_type, 0);
-            const std::uint32_t idesc_pv = idesc_f16(0, 0, 1);  // P and V as fp16
-            const std::uint32_t q_base = smem_u32(smem + kQ);
+            constexpr std::uint32_t in_type = kBf16 ? 1u : 0u;
+            const std::uint32_t idesc_s = idesc_f16(in_type, in_type, 0);
+            const std::uint32_t idesc_pv = idesc_f16(0, 0, 1);  // P and V as fp16, V MN-major
             bool ok = wait(&bars[kBarQ], 0);
-            auto issue_s = [&](int j) {
+            for (int j = 0; ok && j < n_total; ++j) {
                 const int st = j & 1;
+                if (!(ok = wait(&bars[kBarK + st], (j >> 1) & 1))) break;
                 const std::uint32_t k_base = smem_u32(smem + kK0 + st * kTile);
-                const std::uint32_t d = tmem + static_cast<std::uint32_t>(st * 128);
 #pragma unroll
-                for (int k = 0; k < 8; ++k) {
-                    const std::uint32_t off = (k >> 2) * kHalf + (k & 3) * 32;
-                    mma_f16(d, sw128_desc(q_base + off, 16, 1024), sw128_desc(k_base + off, 16, 1024),
-                            idesc_s, k > 0 ? 1u : 0u);
-                }
-                mma_commit(&bars[kBarS + st]);
-                mma_commit(&bars[kBarKFree + st]);
-            };
-            if (ok && (ok = wait(&bars[kBarK], 0))) {
-                tc_fence_after();
-                issue_s(0);
-            }
-            for (int j = 0; ok && j < n_tiles; ++j) {
-                if (j + 1 < n_tiles) {
-                    const int st1 = (j + 1) & 1;
-                    if (!(ok = wait(&bars[kBarK + st1], ((j + 1) >> 1) & 1))) break;
-                    if (j >= 1 && !(ok = wait(&bars[kBarSFree + st1], ((j - 1) >> 1) & 1))) break;
+                for (int t = 0; t < 2; ++t) {
+                    if (j >= ntiles[t]) continue;
+                    // S_t is free once PV_t(j - 1) has consumed P_t.
+                    if (j >= 1 && !(ok = wait(&bars[kBarO + t], (j - 1) & 1))) break;
                     tc_fence_after();
-                    issue_s(j + 1);
-                }
-                if (!(ok = wait(&bars[kBarP], j & 1))) break;
-                if (!(ok = wait(&bars[kBarV + (j & 1)], (j >> 1) & 1))) break;
-                tc_fence_after();
-                const std::uint32_t p_base = smem_u32(smem + kP);
-                const std::uint32_t v_base = smem_u32(smem + kV0 + (j & 1) * kTile);
+                    const std::uint32_t q_base = smem_u32(smem + kQ0 + t * kTile);
+                    const std::uint32_t d = tmem + static_cast<std::uint32_t>(t * 256);
 #pragma unroll
-                for (int k = 0; k < 8; ++k) {
-                    const std::uint32_t a_off = (k >> 2) * kHalf + (k & 3) * 32;
-                    mma_f16(tmem + 256, sw128_desc(p_base + a_off, 16, 1024),
-                            sw128_desc(v_base + k * 2048, kHalf, 1024), idesc_pv, k > 0 ? 1u : 0u);
+                    for (int k = 0; k < 8; ++k) {
+                        const std::uint32_t off = (k >> 2) * kHalf + (k & 3) * 32;
+                        mma_f16(d, sw128_desc(q_base + off, 16, 1024),
+                                sw128_desc(k_base + off, 16, 1024), idesc_s, k > 0 ? 1u : 0u);
+                    }
+                    mma_commit(&bars[kBarS + t]);
                 }
-                mma_commit(&bars[kBarPV]);
-                mma_commit(&bars[kBarVFree + (j & 1)]);
+                if (!ok) break;
+                mma_commit(&bars[kBarKFree + st]);
+                if (kBf16) {
+                    if (!(ok = wait(&bars[kBarVReady + st], (j >> 1) & 1))) break;
+                } else {
+                    if (!(ok = wait(&bars[kBarV + st], (j >> 1) & 1))) break;
+                }
+                const std::uint32_t v_base = smem_u32(smem + kV0 + st * kTile);
+#pragma unroll
+                for (int t = 0; t < 2; ++t) {
+                    if (j >= ntiles[t]) continue;
+                    if (!(ok = wait(&bars[kBarP + t], j & 1))) break;
+                    tc_fence_after();
+                    const std::uint32_t a = tmem + static_cast<std::uint32_t>(t * 256);
+                    const std::uint32_t d = a + 128;
+#pragma unroll
+                    for (int k = 0; k < 8; ++k) {
+                        mma_f16_tmem_a(d, a + k * 8, sw128_desc(v_base + k * 2048, kHalf, 1024),
+                                       idesc_pv, (j > 0 || k > 0) ? 1u : 0u);
+                    }
+                    mma_commit(&bars[kBarO + t]);
+                }
+                if (!ok) break;
+                mma_commit(&bars[kBarVFree + st]);
             }
             // All MMAs issued by this thread complete before TMEM is released.
             mma_commit(&bars[kBarDone]);
             mbar_wait_bounded(&bars[kBarDone], 0, p.error_word);
         }
-    } else {
-        // ------------------------------------------------------------ softmax
-        const int row = threadIdx.x;  // 0..127, TMEM lane = row
-        const std::uint32_t lane_addr = tmem + (static_cast<std::uint32_t>(warp * 32) << 16);
-        const int qpos = start + q_lo + row;  // this row's position in its sequence
-        float o[kD];
-#pragma unroll
-        for (int i = 0; i < kD; ++i) o[i] = 0.0f;
-        float m = -INFINITY;
-        float l = 0.0f;
-        bool ok = true;
-        for (int j = 0; j < n_tiles; ++j) {
-            const int st = j & 1;
-            if (!(ok = warp_ok(wait(&bars[kBarS + st], (j >> 1) & 1)))) break;
-            tc_fence_after();
-            const int key0 = j * kBN;
-            const bool full = key0 + kBN - 1 <= start + q_lo;  // no masking anywhere in the tile
-            const std::uint32_t s_addr = lane_addr + static_cast<std::uint32_t>(st * 128);
-            float mx = -INFINITY;
-#pragma unroll
-            for (int c = 0; c < 4; ++c) {
-                float s[32];
-                tmem_load32(s_addr + c * 32, s);
-#pragma unroll
-                for (int i = 0; i < 32; ++i) {
-                    const bool valid = full || (key0 + c * 32 + i <= qpos);
-                    mx = fmaxf(mx, valid ? s[i] : -INFINITY);
-                }
-            }
-            const float m_new = fmaxf(m, mx * p.scale_log2);
-            const float base = m_new == -INFINITY ? 0.0f : m_new;
-            const float alpha = exp2f(m - base);
-            if (j > 0) {
-                if (!(ok = warp_ok(wait(&bars[kBarPV], (j - 1) & 1)))) break;
-                tc_fence_after();
-#pragma unroll
-                for (int c = 0; c < 4; ++c) {
-                    float pv[32];
-                    tmem_load32(lane_addr + 256 + c * 32, pv);
-#pragma unroll
-                    for (int i = 0; i < 32; ++i) o[c * 32 + i] = (o[c * 32 + i] + pv[i]) * alpha;
-                }
-            }
-            if constexpr (kBf16) {
-                // V arrived as bf16; PV runs with fp16 operands (P needs fp16's
-                // 11-bit significand), so widen V in place: same 16-bit layout.
-                if (!(ok = warp_ok(wait(&bars[kBarV + st], (j >> 1) & 1)))) break;
+    } else if (warp == 10) {
+        // ------------------------------------------------------------ V widening (bf16)
+        if constexpr (kBf16) {
+            for (int j = 0; j < n_total; ++j) {
+                const int st = j & 1;
+                if (!warp_ok(wait(&bars[kBarV + st], (j >> 1) & 1))) break;
                 uint4* v = reinterpret_cast<uint4*>(smem + kV0 + st * kTile);
-                for (int i = row; i < kTile / 16; i += 128) {
+                for (int i = lane; i < kTile / 16; i += 32) {
                     uint4 w = v[i];
                     std::uint32_t* u = reinterpret_cast<std::uint32_t*>(&w);
 #pragma unroll
-                    for (int t = 0; t < 4; ++t) {
-                        const float lo = __uint_as_float(u[t] << 16);
-                        const float hi = __uint_as_float(u[t] & 0xFFFF0000u);
+                    for (int e = 0; e < 4; ++e) {
+                        const float lo = __uint_as_float(u[e] << 16);
+                        const float hi = __uint_as_float(u[e] & 0xFFFF0000u);
                         const __half2 h = __floats2half2_rn(lo, hi);
-                        u[t] = *reinterpret_cast<const std::uint32_t*>(&h);
+                        u[e] = *reinterpret_cast<const std::uint32_t*>(&h);
                     }
                     v[i] = w;
                 }
+                fence_proxy_async_shared();
+                mbar_arrive(&bars[kBarVReady + st]);
             }
-            float sum = 0.0f;
-            unsigned char* prow = smem + kP + row * 128;
+        }
+    } else {
+        // ------------------------------------------------------------ softmax (tiles A, B)
+        const int t = warp >> 2;
+        const int row = threadIdx.x & 127;  // TMEM lane = row of the tile
+        const std::uint32_t lane_addr = tmem + (static_cast<std::uint32_t>((warp & 3) * 32) << 16) +
+                                        static_cast<std::uint32_t>(t * 256);
+        const int n = ntiles[t];
+        const int qpos = start + q_lo + t * kBM + row;  // this row's position in its sequence
+        float m = -INFINITY;  // kept max (log2 units)
+        float l = 0.0f;
+        bool ok = n > 0;
+        for (int j = 0; ok && j < n; ++j) {
+            if (!(ok = warp_ok(wait(&bars[kBarS + t], j & 1)))) break;
+            tc_fence_after();
+            std::uint32_t s[128];
+            tmem_load128(lane_addr, s);
+            const int key0 = j * kBN;
+            // Tiles on the causal diagonal: masked scores become -inf, which
+            // the exponent below turns into p = 0. The branch is uniform per
+            // warp group (it depends on the tile, not the row).
+            if (key0 + kBN - 1 > start + q_lo + t * kBM) {
 #pragma unroll
-            for (int c = 0; c < 4; ++c) {
-                float s[32];
-                tmem_load32(s_addr + c * 32, s);
-#pragma unroll
-                for (int g = 0; g < 4; ++g) {
-                    std::uint32_t packed[4];
-#pragma unroll
-                    for (int t = 0; t < 4; ++t) {
-                        const int i = g * 8 + t * 2;
-                        const bool v0 = full || (key0 + c * 32 + i <= qpos);
-                        const bool v1 = full || (key0 + c * 32 + i + 1 <= qpos);
-                        const float p0 = v0 ? exp2f(s[i] * p.scale_log2 - base) : 0.0f;
-                        const float p1 = v1 ? exp2f(s[i + 1] * p.scale_log2 - base) : 0.0f;
-                        const __half2 h = __floats2half2_rn(p0, p1);
-                        const float2 back = __half22float2(h);
-                        sum += back.x + back.y;  // normalise by what the MMA multiplies
-                        packed[t] = *reinterpret_cast<const std::uint32_t*>(&h);
-                    }
-                    // key chunk (c * 4 + g) of 8 keys: half (chunk / 8), 16-byte slot (chunk % 8)
-                    const int chunk = c * 4 + g;
-                    unsigned char* dst = prow + (chunk >> 3) * kHalf +
-                                         (((chunk & 7) ^ (row & 7)) << 4);
-                    *reinterpret_cast<uint4*>(dst) =
-                        make_uint4(packed[0], packed[1], packed[2], packed[3]);
+                for (int i = 0; i < 128; ++i) {
+                    if (key0 + i > qpos) s[i] = __float_as_uint(-INFINITY);
                 }
             }
-            l = l * alpha + sum;
-            m = m_new;
-            fence_proxy_async_shared();
+            float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+            for (int i = 0; i < 128; i += 4) {
+#pragma unroll
+                for (int u = 0; u < 4; ++u) mx4[u] = fmaxf(mx4[u], __uint_as_float(s[i + u]));
+            }
+            const float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
+            const float m_seen = fmaxf(m, mx * p.scale_log2);
+            if (j == 0) {
+                m = m_seen;
+            } else {
+                const bool grow = m_seen > m + kRescaleThreshold;
+                if (__any_sync(0xffffffffu, grow)) {
+                    // O_t must be complete before it is rescaled in place.
+                    if (!(ok = warp_ok(wait(&bars[kBarO + t], (j - 1) & 1)))) break;
+                    tc_fence_after();
+                    const float alpha = grow ? exp2f(m - m_seen) : 1.0f;
+#pragma unroll
+                    for (int c = 0; c < 4; ++c) {
+                        float o[32];
+                        tmem_load32(lane_addr + 128 + c * 32, o);
+                        std::uint32_t w[32];
+#pragma unroll
+                        for (int i = 0; i < 32; ++i) w[i] = __float_as_uint(o[i] * alpha);
+                        tmem_store32(lane_addr + 128 + c * 32, w);
+                    }
+                    tmem_store_wait();
+                    if (grow) {
+                        l *= alpha;
+                        m = m_seen;
+                    }
+                }
+            }
+            // P = 2^(s * scale - m) in fp16, written over the first 64 columns
+            // of S. Pairs of scores go through one packed f32x2 FMA, then the
+            // hardware ex2; the row sum is kept in fp32 (four pair sums).
+            const std::uint64_t scale2 = pack_f32x2(p.scale_log2, p.scale_log2);
+            const std::uint64_t neg_m2 = pack_f32x2(-m, -m);
+            std::uint64_t sum2[4] = {0, 0, 0, 0};
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+                std::uint32_t packed[16];
+#pragma unroll
+                for (int e = 0; e < 16; ++e) {
+                    const int i = c * 32 + e * 2;
+                    const std::uint64_t x = ffma_f32x2(pack_u32x2(s[i], s[i + 1]), scale2, neg_m2);
+                    const float p0 = ex2_ftz(low_f32(x));
+                    const float p1 = ex2_ftz(high_f32(x));
+                    sum2[e & 3] = fadd_f32x2(sum2[e & 3], pack_f32x2(p0, p1));
+                    const __half2 h = __floats2half2_rn(p0, p1);
+                    packed[e] = *reinterpret_cast<const std::uint32_t*>(&h);
+                }
+                tmem_store16(lane_addr + c * 16, packed);
+            }
+            tmem_store_wait();
+            const std::uint64_t s01 = fadd_f32x2(sum2[0], sum2[1]);
+            const std::uint64_t s23 = fadd_f32x2(sum2[2], sum2[3]);
+            const std::uint64_t s0123 = fadd_f32x2(s01, s23);
+            l += low_f32(s0123) + high_f32(s0123);
             tc_fence_before();
-            mbar_arrive(&bars[kBarSFree + st]);
-            mbar_arrive(&bars[kBarP]);
+            mbar_arrive(&bars[kBarP + t]);
         }
-        if (ok && warp_ok(wait(&bars[kBarPV], (n_tiles - 1) & 1))) {
+        if (ok && warp_ok(wait(&bars[kBarO + t], (n - 1) & 1))) {
             tc_fence_after();
             const float inv = 1.0f / l;
             // Every lane takes part in the TMEM loads (warp-collective); only
             // rows inside the segment store.
-            const bool store = row < rows;
-            float* out = p.out + (static_cast<std::size_t>(offset + q_lo + (store ? row : 0)) *
+            const bool store = row < rows[t];
+            float* out = p.out + (static_cast<std::size_t>(offset + q_lo + t * kBM + (store ? row : 0)) *
                                       p.q_heads + head) * kD;
 #pragma unroll
             for (int c = 0; c < 4; ++c) {
-                float pv[32];
-                tmem_load32(lane_addr + 256 + c * 32, pv);
+                float o[32];
+                tmem_load32(lane_addr + 128 + c * 32, o);
                 if (store) {
 #pragma unroll
                     for (int i = 0; i < 32; i += 4) {
-                        float4 w;
-                        w.x = (o[c * 32 + i] + pv[i]) * inv;
-                        w.y = (o[c * 32 + i + 1] + pv[i + 1]) * inv;
-                        w.z = (o[c * 32 + i + 2] + pv[i + 2]) * inv;
-                        w.w = (o[c * 32 + i + 3] + pv[i + 3]) * inv;
-                        *reinterpret_cast<float4*>(out + c * 32 + i) = w;
+                        *reinterpret_cast<float4*>(out + c * 32 + i) =
+                            make_float4(o[i] * inv, o[i + 1] * inv, o[i + 2] * inv, o[i + 3] * inv);
                     }
                 }
             }
@@ -486,7 +570,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     tc_fence_before();
     __syncthreads();
-    if (warp == 5) {
+    if (warp == 9) {
         __syncwarp();
         tc_fence_after();
         tmem_dealloc(tmem, kTmemCols);
@@ -580,7 +664,7 @@ inline void run_tc_prefill(InferlabCudaKvPool& pool, const void* queries, std::u
         bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
     const cuuint64_t q_dims[3] = {kD, q_heads, static_cast<cuuint64_t>(total_queries)};
     const cuuint64_t q_strides[2] = {kD * 2, static_cast<cuuint64_t>(q_heads) * kD * 2};
-    const cuuint32_t q_box[3] = {64, 1, kBM};
+    const cuuint32_t q_box[3] = {64, 1, kBM};  // one 128-query tile per box
     const CUtensorMap q_map = make_map(q16, type, 3, q_dims, q_strides, q_box);
     const cuuint64_t kv_dims[4] = {kD, kBlockTokens, pool.kv_heads, pool.num_blocks};
     const cuuint64_t kv_strides[3] = {kD * 2, kBlockTokens * kD * 2,
@@ -598,13 +682,13 @@ inline void run_tc_prefill(InferlabCudaKvPool& pool, const void* queries, std::u
     params.num_segments = num_segments;
     params.q_heads = q_heads;
     params.group = q_heads / pool.kv_heads;
-    params.q_tiles = (max_query_count + kBM - 1) / kBM;
+    params.q_blocks = (max_query_count + kQBlock - 1) / kQBlock;
     params.num_blocks = pool.num_blocks;
     params.total_queries = total_queries;
     params.scale_log2 = (1.0f / std::sqrt(static_cast<float>(kD))) * kLog2e;
     params.out = out;
     params.error_word = pool.error_word;
-    const std::uint64_t grid = static_cast<std::uint64_t>(num_segments) * q_heads * params.q_tiles;
+    const std::uint64_t grid = static_cast<std::uint64_t>(num_segments) * q_heads * params.q_blocks;
     if (grid > 0x7FFFFFFFull) throw std::runtime_error("paged prefill grid is too large");
     auto kernel = bf16 ? prefill_tc_kernel<true> : prefill_tc_kernel<false>;
     cuda_check(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemAlloc),

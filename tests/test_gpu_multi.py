@@ -1,0 +1,67 @@
+"""Multi-GPU parity (needs >= 2 GPUs; skipped otherwise).
+
+One long sequence split across two GPUs by contiguous block ranges: each rank
+decodes its range into (m, l, o) partials, the partials are all-gathered over
+NCCL and merged in rank order; the result must equal the whole-context decode
+on one GPU within the fp32 tolerance |a - b| <= 1e-6 + 1e-5 |b|. Ranks are
+spawned processes with a short process-group timeout.
+"""
+import datetime
+import os
+import socket
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+
+def _port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _rank_main(rank, world, port, path):
+    import torch
+    import torch.distributed as dist
+
+    from inferlab_b200 import distributed, workloads as wl
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=60),
+                            device_id=torch.device(f"cuda:{rank}"))
+    try:
+        total = 20000
+        # every rank builds the same full sequence (same seed) so rank 0 can
+        # also decode it whole; each rank then keeps only its own block range
+        full = wl.decode_batch(rank, 77, 1, np.array([total]), 32, 8, 128, wl.KV_BF16,
+                               max_context_len=total)
+        lo, hi = distributed.local_tokens(total, 16, world, rank)
+        blocks = full.block_tables[:, lo // 16:(hi + 15) // 16].contiguous()
+        merged = distributed.decode_split_sequence(full.pool, full.queries, blocks, hi - lo)
+        whole = full.pool.decode(full.queries, full.block_tables, full.context_lens, total)
+        full.pool.synchronize()
+        if rank == 0:
+            np.save(path, np.stack([merged.cpu().numpy(), whole.cpu().numpy()]))
+        full.pool.close()
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+def test_split_sequence_over_nccl_matches_single_gpu(tmp_path):
+    import torch
+    import torch.multiprocessing as mp
+
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    path = str(tmp_path / "out.npy")
+    mp.start_processes(_rank_main, args=(2, _port(), path), nprocs=2, start_method="spawn",
+                       join=True)
+    merged, whole = np.load(path)
+    err = np.abs(merged.astype(np.float64) - whole)
+    assert np.all(err <= 1e-6 + 1e-5 * np.abs(whole)), float(err.max())
