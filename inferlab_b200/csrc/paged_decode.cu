@@ -534,7 +534,9 @@ DecodePlan plan_decode(std::uint32_t num_seqs, std::uint32_t kv_heads,
         bps = static_cast<std::uint32_t>((max_blocks + splits - 1) / splits);
         bps = std::max<std::uint32_t>(bps, 8);
     }
-    bps = std::min<std::uint32_t>(std::max<std::uint32_t>(bps, 1), kMaxBlocksPerSplit);
+    // Splits of at most 256 blocks (4096 tokens) keep CTAs short enough to
+    // balance; only contexts beyond kMaxSplits * 256 blocks get longer ones.
+    bps = std::min<std::uint32_t>(std::max<std::uint32_t>(bps, 1), 256);
     // The fused merge keeps one weight per (q-head, split) in the tile area:
     // at most kMaxSplits splits per context.
     bps = std::max<std::uint32_t>(bps, (max_blocks + kMaxSplits - 1) / kMaxSplits);

@@ -5,7 +5,7 @@
 // legal_sources (kernels/attention_cpu.cpp:113-123): query i of a segment that
 // starts at position P sees keys [0, P + i].
 //
-// Roles (352 threads):
+// Roles (384 threads):
 //   warps 0-3 / 4-7  softmax for tile A / B: thread t owns query row t. Per
 //              128-key tile it reads its S row from TMEM once (tcgen05.ld
 //              32x32b.x128), masks, takes the row max, computes fp16
@@ -21,11 +21,12 @@
 //              blocks of K and of V, each a box of the 4-D map over the arena
 //              [block][kv_head][slot][128] at the block id the table names
 //              (no multicast).
-//   warp 9     MMA issuer: S_t = Q_t K^T (M=N=128, K=128, f16/bf16, fp32 in
-//              TMEM) for both tiles, then O_t += P_t V (P from TMEM, V an
-//              MN-major shared-memory operand), so the tensor core works on one
-//              tile while the other tile's softmax runs.
-//   warp 10    (bf16 pools) widens each V tile from bf16 to fp16 in shared
+//   warps 9/10 MMA issuers, one thread per tile: S_t = Q_t K^T (M=N=128,
+//              K=128, f16/bf16, fp32 in TMEM), then O_t += P_t V (P from TMEM,
+//              V an MN-major shared-memory operand). Each tile runs its own
+//              S -> softmax -> PV chain, so the tensor core works on one tile
+//              while the other tile's softmax runs.
+//   warp 11    (bf16 pools) widens each V tile from bf16 to fp16 in shared
 //              memory before its PV, so P keeps fp16's 11-bit significand.
 // TMEM (512 columns): tile t uses [256t, 256t + 128) for S / P and
 // [256t + 128, 256t + 256) for O.
@@ -52,7 +53,7 @@ constexpr int kQBlock = 2 * kBM;         // queries per CTA (tiles A and B)
 constexpr int kBN = 128;                 // keys per K/V tile
 constexpr int kD = 128;
 constexpr int kBlockTokens = 16;
-constexpr int kThreads = 352;
+constexpr int kThreads = 384;
 constexpr int kHalf = 16384;             // one 64-column half of a 128 x 128 16-bit tile
 constexpr int kTile = 2 * kHalf;         // 32 KB
 constexpr int kQ0 = 0;                   // Q tiles A, B
@@ -75,7 +76,7 @@ enum Bar : int {
     kBarP = 11,      // +tile, 128 arrivals
     kBarO = 13,      // +tile
     kBarVReady = 15, // +stage, 32 arrivals (bf16 widening)
-    kBarDone = 17,
+    kBarDone = 17,   // +tile
 };
 
 struct Params {
@@ -305,6 +306,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             std::uint32_t arrivals = 1;
             if (b == kBarP || b == kBarP + 1) arrivals = 128;
             if (b == kBarVReady || b == kBarVReady + 1) arrivals = 32;
+            if (b == kBarKFree || b == kBarKFree + 1 || b == kBarVFree || b == kBarVFree + 1) {
+                arrivals = 2;  // one commit from each tile's issuer
+            }
             mbar_init(&bars[b], arrivals);
         }
         *abort = 0;
@@ -378,63 +382,63 @@ __global__ void __launch_bounds__(kThreads, 1)
                 mbar_wait_bounded(&bars[bar], (j >> 1) & 1, p.error_word);
             }
         }
-    } else if (warp == 9) {
-        // ------------------------------------------------------------ MMA issuer
+    } else if (warp == 9 || warp == 10) {
+        // ------------------------------------------------------------ MMA issuers
+        // One issuing thread per tile, so each tile runs its own
+        // S -> softmax -> PV chain and the tensor core interleaves the two.
+        // Both issuers walk every K/V tile in order and arrive on the
+        // K/V-free barriers (two arrivals each), the tile that needs fewer
+        // K/V tiles with empty commits, which arrive at once.
+        const int t = warp - 9;
         if (lane == 0) {
             constexpr std::uint32_t in_type = kBf16 ? 1u : 0u;
             const std::uint32_t idesc_s = idesc_f16(in_type, in_type, 0);
             const std::uint32_t idesc_pv = idesc_f16(0, 0, 1);  // P and V as fp16, V MN-major
+            const std::uint32_t q_base = smem_u32(smem + kQ0 + t * kTile);
+            const std::uint32_t s_tmem = tmem + static_cast<std::uint32_t>(t * 256);
+            const int n = ntiles[t];
             bool ok = wait(&bars[kBarQ], 0);
             for (int j = 0; ok && j < n_total; ++j) {
                 const int st = j & 1;
                 if (!(ok = wait(&bars[kBarK + st], (j >> 1) & 1))) break;
-                const std::uint32_t k_base = smem_u32(smem + kK0 + st * kTile);
-#pragma unroll
-                for (int t = 0; t < 2; ++t) {
-                    if (j >= ntiles[t]) continue;
+                if (j < n) {
                     // S_t is free once PV_t(j - 1) has consumed P_t.
                     if (j >= 1 && !(ok = wait(&bars[kBarO + t], (j - 1) & 1))) break;
                     tc_fence_after();
-                    const std::uint32_t q_base = smem_u32(smem + kQ0 + t * kTile);
-                    const std::uint32_t d = tmem + static_cast<std::uint32_t>(t * 256);
+                    const std::uint32_t k_base = smem_u32(smem + kK0 + st * kTile);
 #pragma unroll
                     for (int k = 0; k < 8; ++k) {
                         const std::uint32_t off = (k >> 2) * kHalf + (k & 3) * 32;
-                        mma_f16(d, sw128_desc(q_base + off, 16, 1024),
+                        mma_f16(s_tmem, sw128_desc(q_base + off, 16, 1024),
                                 sw128_desc(k_base + off, 16, 1024), idesc_s, k > 0 ? 1u : 0u);
                     }
                     mma_commit(&bars[kBarS + t]);
                 }
-                if (!ok) break;
                 mma_commit(&bars[kBarKFree + st]);
                 if (kBf16) {
                     if (!(ok = wait(&bars[kBarVReady + st], (j >> 1) & 1))) break;
                 } else {
                     if (!(ok = wait(&bars[kBarV + st], (j >> 1) & 1))) break;
                 }
-                const std::uint32_t v_base = smem_u32(smem + kV0 + st * kTile);
-#pragma unroll
-                for (int t = 0; t < 2; ++t) {
-                    if (j >= ntiles[t]) continue;
+                if (j < n) {
                     if (!(ok = wait(&bars[kBarP + t], j & 1))) break;
                     tc_fence_after();
-                    const std::uint32_t a = tmem + static_cast<std::uint32_t>(t * 256);
-                    const std::uint32_t d = a + 128;
+                    const std::uint32_t v_base = smem_u32(smem + kV0 + st * kTile);
 #pragma unroll
                     for (int k = 0; k < 8; ++k) {
-                        mma_f16_tmem_a(d, a + k * 8, sw128_desc(v_base + k * 2048, kHalf, 1024),
-                                       idesc_pv, (j > 0 || k > 0) ? 1u : 0u);
+                        mma_f16_tmem_a(s_tmem + 128, s_tmem + k * 8,
+                                       sw128_desc(v_base + k * 2048, kHalf, 1024), idesc_pv,
+                                       (j > 0 || k > 0) ? 1u : 0u);
                     }
                     mma_commit(&bars[kBarO + t]);
                 }
-                if (!ok) break;
                 mma_commit(&bars[kBarVFree + st]);
             }
             // All MMAs issued by this thread complete before TMEM is released.
-            mma_commit(&bars[kBarDone]);
-            mbar_wait_bounded(&bars[kBarDone], 0, p.error_word);
+            mma_commit(&bars[kBarDone + t]);
+            mbar_wait_bounded(&bars[kBarDone + t], 0, p.error_word);
         }
-    } else if (warp == 10) {
+    } else if (warp == 11) {
         // ------------------------------------------------------------ V widening (bf16)
         if constexpr (kBf16) {
             for (int j = 0; j < n_total; ++j) {
