@@ -226,6 +226,34 @@ __device__ __forceinline__ bool mbar_try_wait(std::uint64_t* bar, std::uint32_t 
     return done != 0;
 }
 
+// Non-blocking probe of an mbarrier phase (never suspends the thread).
+__device__ __forceinline__ bool mbar_test_wait(std::uint64_t* bar, std::uint32_t parity) {
+    std::uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(done)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return done != 0;
+}
+
+// 16-byte global -> shared copies through the LSU (cp.async, L2 only), in
+// commit groups. Used where many small pieces are gathered: the TMA unit
+// spends ~90 cycles on each 2 KB box, the LSU path streams ~3x faster with
+// a few warps issuing.
+__device__ __forceinline__ void cp_async16(std::uint32_t dst, const void* src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() {
+    asm volatile("cp.async.commit_group;" ::: "memory");
+}
+template <int N>
+__device__ __forceinline__ void cp_async_wait_group() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
 __device__ __forceinline__ std::uint64_t global_timer_ns() {
     std::uint64_t t;
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
@@ -296,6 +324,37 @@ __device__ __forceinline__ float ex2_ftz(float x) {
     float y;
     asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
     return y;
+}
+
+// max(a, b, c) in one instruction (three-input max.f32, sm_100).
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+    float r;
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+    return r;
+}
+
+// 2^x for a pair of x <= 8 on the FMA / integer pipes instead of the MUFU
+// unit: x is clamped to >= -126, split as x = n + f with n the nearest
+// integer (the 1.5 * 2^23 rounding trick) and f in [-0.5, 0.5]; 2^f is a
+// cubic fitted to 2^f on [-0.5, 0.5] by reweighted least squares on Chebyshev
+// nodes (max relative error 1.5e-4 evaluated in fp32, below fp16's 4.9e-4
+// rounding step), and 2^n is added into the exponent field. Used for a share
+// of the softmax exponentials so the MUFU unit is not the bottleneck.
+__device__ __forceinline__ std::uint64_t ex2_poly_f32x2(float x0, float x1) {
+    x0 = fmaxf(x0, -126.0f);
+    x1 = fmaxf(x1, -126.0f);
+    const std::uint64_t x = pack_f32x2(x0, x1);
+    const std::uint64_t magic = pack_f32x2(12582912.0f, 12582912.0f);
+    const std::uint64_t t = fadd_f32x2(x, magic);
+    const std::uint64_t n = fadd_f32x2(t, pack_f32x2(-12582912.0f, -12582912.0f));
+    const std::uint64_t f = ffma_f32x2(n, pack_f32x2(-1.0f, -1.0f), x);
+    std::uint64_t p = ffma_f32x2(pack_f32x2(0.05517149344086647f, 0.05517149344086647f), f,
+                                 pack_f32x2(0.2426111102104187f, 0.2426111102104187f));
+    p = ffma_f32x2(p, f, pack_f32x2(0.6932610273361206f, 0.6932610273361206f));
+    p = ffma_f32x2(p, f, pack_f32x2(0.9999280571937561f, 0.9999280571937561f));
+    const std::uint32_t lo = __float_as_uint(low_f32(p)) + (__float_as_uint(low_f32(t)) << 23);
+    const std::uint32_t hi = __float_as_uint(high_f32(p)) + (__float_as_uint(high_f32(t)) << 23);
+    return pack_u32x2(lo, hi);
 }
 
 __device__ __forceinline__ float warp_max(float v) {

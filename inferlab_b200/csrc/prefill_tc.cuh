@@ -16,16 +16,19 @@
 //              grows by more than 2^8, so probabilities relative to the kept
 //              max stay <= 256 (exact in fp16's range) and the result is the
 //              same online-softmax recurrence (kernels/attention_cpu.cpp:364-386).
-//   warp 8     TMA producer: both Q tiles once (3-D map over
-//              [tokens][q_heads][128]), then per 128-key tile eight 16-token
-//              blocks of K and of V, each a box of the 4-D map over the arena
-//              [block][kv_head][slot][128] at the block id the table names
-//              (no multicast).
-//   warps 9/10 MMA issuers, one thread per tile: S_t = Q_t K^T (M=N=128,
-//              K=128, f16/bf16, fp32 in TMEM), then O_t += P_t V (P from TMEM,
-//              V an MN-major shared-memory operand). Each tile runs its own
-//              S -> softmax -> PV chain, so the tensor core works on one tile
-//              while the other tile's softmax runs.
+//              Before releasing P_t(j) the tile's warps check that V(j) and,
+//              when the tile continues, K(j + 1) are resident.
+//   warp 8     both Q tiles by TMA (3-D map over [tokens][q_heads][128]), then
+//              the K tiles: per 128-key tile the eight 16-token blocks the
+//              table names, gathered with 16-byte cp.async into the 128-byte
+//              swizzled layout, block ids read one tile ahead.
+//   warp 9     MMA issuer (one thread): S_t = Q_t K^T (M=N=128, K=128,
+//              f16/bf16, fp32 in TMEM) and O_t += P_t V (P from TMEM, V an
+//              MN-major shared-memory operand). MMAs of one thread run in
+//              issue order, so S_t(j + 1) follows PV_t(j) without a wait; the
+//              order PV_A, S_A, PV_B, S_B lets one tile's softmax run while the
+//              tensor core works on the other tile.
+//   warp 10    the V tiles, gathered like K.
 //   warp 11    (bf16 pools) widens each V tile from bf16 to fp16 in shared
 //              memory before its PV, so P keeps fp16's 11-bit significand.
 // TMEM (512 columns): tile t uses [256t, 256t + 128) for S / P and
@@ -53,14 +56,14 @@ constexpr int kQBlock = 2 * kBM;         // queries per CTA (tiles A and B)
 constexpr int kBN = 128;                 // keys per K/V tile
 constexpr int kD = 128;
 constexpr int kBlockTokens = 16;
-constexpr int kThreads = 384;
+constexpr int kThreads = 384;  // 8 softmax warps, K and V producers, MMA issuer, V widening
 constexpr int kHalf = 16384;             // one 64-column half of a 128 x 128 16-bit tile
 constexpr int kTile = 2 * kHalf;         // 32 KB
 constexpr int kQ0 = 0;                   // Q tiles A, B
 constexpr int kK0 = 2 * kTile;           // two K stages
 constexpr int kV0 = kK0 + 2 * kTile;     // two V stages
 constexpr int kBars = kV0 + 2 * kTile;   // 192 KB
-constexpr int kNumBars = 20;
+constexpr int kNumBars = 18;
 constexpr int kSmemBytes = kBars + kNumBars * 8 + 64;
 constexpr int kSmemAlloc = kSmemBytes + 1024;  // slack to align the base to 1024 B
 constexpr uint32_t kTmemCols = 512;
@@ -73,13 +76,16 @@ enum Bar : int {
     kBarKFree = 5,   // +stage
     kBarVFree = 7,   // +stage
     kBarS = 9,       // +tile
-    kBarP = 11,      // +tile, 128 arrivals
+    kBarP = 11,      // +tile, 4 arrivals (one per softmax warp)
     kBarO = 13,      // +tile
-    kBarVReady = 15, // +stage, 32 arrivals (bf16 widening)
-    kBarDone = 17,   // +tile
+    kBarVReady = 15, // +stage (bf16 widening)
+    kBarDone = 17,
 };
 
 struct Params {
+    const unsigned char* key_arena;    // [block][kv_head][slot][128], 16-bit elements
+    const unsigned char* value_arena;
+    std::uint32_t kv_heads;
     const std::int32_t* tables;
     std::uint32_t max_blocks;
     const std::int32_t* starts;
@@ -250,7 +256,11 @@ struct Waiter {
     int* abort;
     std::uint32_t* error_word;
     // Bounded wait that fails fast once any role of the CTA has given up.
+    // The first probe of the barrier comes before the abort flag is read:
+    // shared-memory accesses are slow while the tensor core streams operands,
+    // so a phase that is already complete costs one access.
     __device__ __forceinline__ bool operator()(std::uint64_t* bar, std::uint32_t parity) const {
+        if (mbar_try_wait(bar, parity)) return true;
         if (*reinterpret_cast<volatile int*>(abort)) return false;
         if (mbar_wait_bounded(bar, parity, error_word, 1000000000ull)) return true;
         *reinterpret_cast<volatile int*>(abort) = 1;
@@ -260,9 +270,7 @@ struct Waiter {
 
 template <bool kBf16>
 __global__ void __launch_bounds__(kThreads, 1)
-    prefill_tc_kernel(const __grid_constant__ CUtensorMap q_map,
-                      const __grid_constant__ CUtensorMap k_map,
-                      const __grid_constant__ CUtensorMap v_map, const Params p) {
+    prefill_tc_kernel(const __grid_constant__ CUtensorMap q_map, const Params p) {
     extern __shared__ unsigned char smem_raw[];
     unsigned char* smem = reinterpret_cast<unsigned char*>(
         (reinterpret_cast<std::uintptr_t>(smem_raw) + 1023) & ~static_cast<std::uintptr_t>(1023));
@@ -304,11 +312,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (threadIdx.x == 0) {
         for (int b = 0; b < kNumBars; ++b) {
             std::uint32_t arrivals = 1;
-            if (b == kBarP || b == kBarP + 1) arrivals = 128;
-            if (b == kBarVReady || b == kBarVReady + 1) arrivals = 32;
-            if (b == kBarKFree || b == kBarKFree + 1 || b == kBarVFree || b == kBarVFree + 1) {
-                arrivals = 2;  // one commit from each tile's issuer
-            }
+            if (b == kBarP || b == kBarP + 1) arrivals = 4;  // the tile's four softmax warps
             mbar_init(&bars[b], arrivals);
         }
         *abort = 0;
@@ -324,9 +328,19 @@ __global__ void __launch_bounds__(kThreads, 1)
     const std::uint32_t tmem = *tmem_slot;
     const Waiter wait{abort, p.error_word};
 
-    if (warp == 8) {
-        // ------------------------------------------------------------ producer
-        if (lane == 0) {
+    if (warp == 8 || warp == 10) {
+        // ------------------------------------------------------------ K / V producers
+        // Warp 8 gathers K tiles, warp 10 V tiles, 16 bytes a lane per
+        // cp.async (one 2 KB TMA box per block and half costs the TMA unit
+        // ~90 cycles; the LSU path keeps up with the tensor core). Lane-chunk
+        // map of a 128-key tile: chunk = lane + 32 i (i < 64) is bytes
+        // [16 (chunk & 15), +16) of key row chunk >> 4, i.e. row 2i + lane / 16
+        // of block i / 8; it lands in 64-column half (chunk >> 3) & 1 at
+        // row * 128 + 16 ((chunk & 7) ^ (row & 7)) - the 128-byte swizzle the
+        // MMA descriptors name. A tile is announced on its full barrier once
+        // the warp's copies have landed (wait_group, proxy fence, one arrival).
+        const bool is_k = warp == 8;
+        if (is_k && lane == 0) {
             mbar_arrive_expect_tx(&bars[kBarQ], 2 * kTile);
 #pragma unroll
             for (int t = 0; t < 2; ++t) {
@@ -335,108 +349,144 @@ __global__ void __launch_bounds__(kThreads, 1)
                 tma_load_3d(smem + kQ0 + t * kTile + kHalf, &q_map, 64, static_cast<int>(head),
                             offset + q_lo + t * kBM, &bars[kBarQ]);
             }
-            int issued = 0;
-            for (int j = 0; j < n_total; ++j) {
-                const int st = j & 1;
-                if (j >= 2 && !wait(&bars[kBarKFree + st], ((j >> 1) - 1) & 1)) break;
-                std::int32_t ids[8];
-#pragma unroll
-                for (int b = 0; b < 8; ++b) {
-                    const int logical = j * 8 + b;
-                    std::int32_t id = table[logical < nblk_total ? logical : 0];
-                    if (id < 0 || static_cast<std::uint64_t>(id) >= p.num_blocks) {
-                        flag_error(p.error_word, kErrBadBlock);
-                        id = 0;
-                    }
-                    ids[b] = id;
-                }
-                unsigned char* kdst = smem + kK0 + st * kTile;
-                mbar_arrive_expect_tx(&bars[kBarK + st], kTile);
-#pragma unroll
-                for (int b = 0; b < 8; ++b) {
-                    tma_load_4d(kdst + b * 2048, &k_map, 0, 0, static_cast<int>(kv_head), ids[b],
-                                &bars[kBarK + st]);
-                    tma_load_4d(kdst + kHalf + b * 2048, &k_map, 64, 0, static_cast<int>(kv_head),
-                                ids[b], &bars[kBarK + st]);
-                }
-                if (j >= 2 && !wait(&bars[kBarVFree + st], ((j >> 1) - 1) & 1)) {
-                    issued = j * 2 + 1;
-                    break;
-                }
-                unsigned char* vdst = smem + kV0 + st * kTile;
-                mbar_arrive_expect_tx(&bars[kBarV + st], kTile);
-#pragma unroll
-                for (int b = 0; b < 8; ++b) {
-                    tma_load_4d(vdst + b * 2048, &v_map, 0, 0, static_cast<int>(kv_head), ids[b],
-                                &bars[kBarV + st]);
-                    tma_load_4d(vdst + kHalf + b * 2048, &v_map, 64, 0, static_cast<int>(kv_head),
-                                ids[b], &bars[kBarV + st]);
-                }
-                issued = j * 2 + 2;
-            }
-            // Drain: the last copy issued into each barrier must land before exit.
-            mbar_wait_bounded(&bars[kBarQ], 0, p.error_word);
-            for (int c = issued - 1; c >= 0 && c >= issued - 4; --c) {
-                const int j = c >> 1;
-                const int bar = (c & 1) ? kBarV + (j & 1) : kBarK + (j & 1);
-                mbar_wait_bounded(&bars[bar], (j >> 1) & 1, p.error_word);
-            }
         }
-    } else if (warp == 9 || warp == 10) {
-        // ------------------------------------------------------------ MMA issuers
-        // One issuing thread per tile, so each tile runs its own
-        // S -> softmax -> PV chain and the tensor core interleaves the two.
-        // Both issuers walk every K/V tile in order and arrive on the
-        // K/V-free barriers (two arrivals each), the tile that needs fewer
-        // K/V tiles with empty commits, which arrive at once.
-        const int t = warp - 9;
+        const unsigned char* arena = (is_k ? p.key_arena : p.value_arena) +
+                                     static_cast<std::size_t>(kv_head) * (kBlockTokens * kD * 2) +
+                                     static_cast<std::size_t>((lane >> 4) * 256 + (lane & 15) * 16);
+        const std::size_t block_bytes = static_cast<std::size_t>(p.kv_heads) * (kBlockTokens * kD * 2);
+        const std::uint32_t stage0 = smem_u32(smem + (is_k ? kK0 : kV0));
+        const int full_bar = is_k ? kBarK : kBarV;
+        const int free_bar = is_k ? kBarKFree : kBarVFree;
+        // Shared-memory offset of lane's chunk in row pair i (rows 2i, 2i + 1).
+        const int half = (lane >> 3) & 1;
+        const int c = lane & 7;
+        auto read_id = [&](int j) {
+            const int logical = j * 8 + (lane & 7);
+            return table[logical < nblk_total ? logical : 0];
+        };
+        auto announce = [&](int jj) {
+            fence_proxy_async_shared();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&bars[full_bar + (jj & 1)]);
+        };
+        std::int32_t next_id = read_id(0);
+        int pending = -1;  // tile whose copies are in flight, not yet announced
+        for (int j = 0; j < n_total; ++j) {
+            const int st = j & 1;
+            std::int32_t id = next_id;
+            if (id < 0 || static_cast<std::uint64_t>(id) >= p.num_blocks) {
+                if (lane < 8) flag_error(p.error_word, kErrBadBlock);
+                id = 0;
+            }
+            if (j + 1 < n_total) next_id = read_id(j + 1);
+            if (j >= 2) {
+                const std::uint32_t parity = ((j >> 1) - 1) & 1;
+                if (!warp_ok(mbar_test_wait(&bars[free_bar + st], parity))) {
+                    // About to block: announce what has been copied first.
+                    if (pending >= 0) {
+                        cp_async_wait_group<0>();
+                        announce(pending);
+                        pending = -1;
+                    }
+                    if (!warp_ok(wait(&bars[free_bar + st], parity))) break;
+                }
+            }
+            const std::uint32_t dst = stage0 + static_cast<std::uint32_t>(st * kTile + half * kHalf);
+#pragma unroll
+            for (int b = 0; b < 8; ++b) {
+                const unsigned char* src =
+                    arena + static_cast<std::size_t>(__shfl_sync(0xffffffffu, id, b)) * block_bytes;
+#pragma unroll
+                for (int r = 0; r < 8; ++r) {
+                    const int row = b * 16 + r * 2 + (lane >> 4);
+                    cp_async16(dst + static_cast<std::uint32_t>(row * 128 + ((c ^ (row & 7)) << 4)),
+                               src + r * 512);
+                }
+            }
+            cp_async_commit();
+            if (pending >= 0) {
+                cp_async_wait_group<1>();
+                announce(pending);
+            }
+            pending = j;
+        }
+        cp_async_wait_group<0>();
+        if (pending >= 0) announce(pending);
+    } else if (warp == 9) {
+        // ------------------------------------------------------------ MMA issuer
+        // tcgen05.mma operations from one thread run in issue order, so
+        // S_t(j + 1) may be issued right behind PV_t(j): it overwrites the S/P
+        // columns only after PV_t(j) has read P_t(j). Issue order per K/V
+        // tile j: PV_A(j), S_A(j + 1), PV_B(j), S_B(j + 1) - tile A's softmax
+        // runs while the tensor core works on tile B and the other way round.
+        //
+        // Every mbarrier wait in this thread stalls the tensor pipe (measured:
+        // 70-300 cycles of idle tensor core per wait, even on a completed
+        // phase), so the issuer waits on P alone. The softmax warps of tile t
+        // arrive on P_t(j) only after V(j) (widened, for bf16) and, when the
+        // tile continues, K(j + 1) are resident. Descriptors are built once;
+        // the K steps add constants to them.
         if (lane == 0) {
             constexpr std::uint32_t in_type = kBf16 ? 1u : 0u;
             const std::uint32_t idesc_s = idesc_f16(in_type, in_type, 0);
             const std::uint32_t idesc_pv = idesc_f16(0, 0, 1);  // P and V as fp16, V MN-major
-            const std::uint32_t q_base = smem_u32(smem + kQ0 + t * kTile);
-            const std::uint32_t s_tmem = tmem + static_cast<std::uint32_t>(t * 256);
-            const int n = ntiles[t];
-            bool ok = wait(&bars[kBarQ], 0);
+            // Scalars, not arrays indexed at run time (those would live in local memory).
+            const std::uint64_t q_desc0 = sw128_desc(smem_u32(smem + kQ0), 16, 1024);
+            const std::uint64_t q_desc1 = sw128_desc(smem_u32(smem + kQ0 + kTile), 16, 1024);
+            const std::uint64_t k_desc0 = sw128_desc(smem_u32(smem + kK0), 16, 1024);
+            const std::uint64_t k_desc1 = sw128_desc(smem_u32(smem + kK0 + kTile), 16, 1024);
+            const std::uint64_t v_desc0 = sw128_desc(smem_u32(smem + kV0), kHalf, 1024);
+            const std::uint64_t v_desc1 = sw128_desc(smem_u32(smem + kV0 + kTile), kHalf, 1024);
+            // S_t = Q_t K(j)^T: 8 K steps of 16; step k starts (k & 3) * 32 B
+            // into the (k >> 2)-th 64-column half (descriptor address unit 16 B).
+            auto issue_s = [&](int t, int j) {
+                const std::uint64_t a = t ? q_desc1 : q_desc0;
+                const std::uint64_t b = (j & 1) ? k_desc1 : k_desc0;
+                const std::uint32_t d = tmem + static_cast<std::uint32_t>(t * 256);
+#pragma unroll
+                for (int k = 0; k < 8; ++k) {
+                    const std::uint64_t off = static_cast<std::uint64_t>(((k >> 2) * kHalf + (k & 3) * 32) >> 4);
+                    mma_f16(d, a + off, b + off, idesc_s, k > 0 ? 1u : 0u);
+                }
+                mma_commit(&bars[kBarS + t]);
+            };
+            bool ok = wait(&bars[kBarQ], 0) && wait(&bars[kBarK], 0);
+            if (ok) {
+                tc_fence_after();
+                for (int t = 0; t < 2; ++t) {
+                    if (ntiles[t] > 0) issue_s(t, 0);
+                }
+                mma_commit(&bars[kBarKFree]);
+            }
             for (int j = 0; ok && j < n_total; ++j) {
                 const int st = j & 1;
-                if (!(ok = wait(&bars[kBarK + st], (j >> 1) & 1))) break;
-                if (j < n) {
-                    // S_t is free once PV_t(j - 1) has consumed P_t.
-                    if (j >= 1 && !(ok = wait(&bars[kBarO + t], (j - 1) & 1))) break;
-                    tc_fence_after();
-                    const std::uint32_t k_base = smem_u32(smem + kK0 + st * kTile);
-#pragma unroll
-                    for (int k = 0; k < 8; ++k) {
-                        const std::uint32_t off = (k >> 2) * kHalf + (k & 3) * 32;
-                        mma_f16(s_tmem, sw128_desc(q_base + off, 16, 1024),
-                                sw128_desc(k_base + off, 16, 1024), idesc_s, k > 0 ? 1u : 0u);
-                    }
-                    mma_commit(&bars[kBarS + t]);
-                }
-                mma_commit(&bars[kBarKFree + st]);
-                if (kBf16) {
-                    if (!(ok = wait(&bars[kBarVReady + st], (j >> 1) & 1))) break;
-                } else {
-                    if (!(ok = wait(&bars[kBarV + st], (j >> 1) & 1))) break;
-                }
-                if (j < n) {
+                const std::uint64_t vb = st ? v_desc1 : v_desc0;
+                for (int t = 0; t < 2; ++t) {
+                    if (j >= ntiles[t]) continue;
                     if (!(ok = wait(&bars[kBarP + t], j & 1))) break;
                     tc_fence_after();
-                    const std::uint32_t v_base = smem_u32(smem + kV0 + st * kTile);
+                    const std::uint32_t s_tmem = tmem + static_cast<std::uint32_t>(t * 256);
 #pragma unroll
                     for (int k = 0; k < 8; ++k) {
+                        // P columns [8k, 8k + 8) hold keys [16k, 16k + 16) as f16 pairs;
+                        // V rows [16k, 16k + 16) start 2048 B further per step.
                         mma_f16_tmem_a(s_tmem + 128, s_tmem + k * 8,
-                                       sw128_desc(v_base + k * 2048, kHalf, 1024), idesc_pv,
+                                       vb + static_cast<std::uint64_t>((k * 2048) >> 4), idesc_pv,
                                        (j > 0 || k > 0) ? 1u : 0u);
                     }
                     mma_commit(&bars[kBarO + t]);
+                    // A commit tracks every earlier MMA of this thread, so V(j)
+                    // is released right after the last PV that reads it, before
+                    // the next S is queued behind it.
+                    if (t == 1 || j >= ntiles[1]) mma_commit(&bars[kBarVFree + st]);
+                    if (j + 1 < ntiles[t]) issue_s(t, j + 1);
                 }
-                mma_commit(&bars[kBarVFree + st]);
+                if (!ok) break;
+                if (j + 1 < n_total) mma_commit(&bars[kBarKFree + ((j + 1) & 1)]);
             }
             // All MMAs issued by this thread complete before TMEM is released.
-            mma_commit(&bars[kBarDone + t]);
-            mbar_wait_bounded(&bars[kBarDone + t], 0, p.error_word);
+            mma_commit(&bars[kBarDone]);
+            mbar_wait_bounded(&bars[kBarDone], 0, p.error_word);
         }
     } else if (warp == 11) {
         // ------------------------------------------------------------ V widening (bf16)
@@ -458,7 +508,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                     v[i] = w;
                 }
                 fence_proxy_async_shared();
-                mbar_arrive(&bars[kBarVReady + st]);
+                // One arrival per warp: 32 arrivals on one mbarrier word
+                // serialise and delay the phase by about a thousand cycles.
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&bars[kBarVReady + st]);
             }
         }
     } else {
@@ -473,6 +526,16 @@ __global__ void __launch_bounds__(kThreads, 1)
         float l = 0.0f;
         bool ok = n > 0;
         for (int j = 0; ok && j < n; ++j) {
+            // PV_t(j) reads V(j) and S_t(j + 1) reads K(j + 1): both must be
+            // resident before P_t(j) releases the issuer (which waits on P
+            // only). Checked while S_t(j) is still being computed; both
+            // copies were issued about a step earlier.
+            if (kBf16) {
+                if (!(ok = warp_ok(wait(&bars[kBarVReady + (j & 1)], (j >> 1) & 1)))) break;
+            } else {
+                if (!(ok = warp_ok(wait(&bars[kBarV + (j & 1)], (j >> 1) & 1)))) break;
+            }
+            if (j + 1 < n && !(ok = warp_ok(wait(&bars[kBarK + ((j + 1) & 1)], ((j + 1) >> 1) & 1)))) break;
             if (!(ok = warp_ok(wait(&bars[kBarS + t], j & 1)))) break;
             tc_fence_after();
             std::uint32_t s[128];
@@ -487,13 +550,18 @@ __global__ void __launch_bounds__(kThreads, 1)
                     if (key0 + i > qpos) s[i] = __float_as_uint(-INFINITY);
                 }
             }
-            float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+            // Row max with the three-input max (two new scores per
+            // instruction), four independent chains.
+            float mx4[4] = {__uint_as_float(s[0]), __uint_as_float(s[1]), __uint_as_float(s[2]),
+                            __uint_as_float(s[3])};
 #pragma unroll
-            for (int i = 0; i < 128; i += 4) {
+            for (int i = 4; i < 128; i += 8) {
 #pragma unroll
-                for (int u = 0; u < 4; ++u) mx4[u] = fmaxf(mx4[u], __uint_as_float(s[i + u]));
+                for (int u = 0; u < 4; ++u) {
+                    mx4[u] = fmax3(mx4[u], __uint_as_float(s[i + 2 * u]), __uint_as_float(s[i + 2 * u + 1]));
+                }
             }
-            const float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
+            const float mx = fmax3(mx4[0], mx4[1], fmaxf(mx4[2], mx4[3]));
             const float m_seen = fmaxf(m, mx * p.scale_log2);
             if (j == 0) {
                 m = m_seen;
@@ -521,8 +589,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
             }
             // P = 2^(s * scale - m) in fp16, written over the first 64 columns
-            // of S. Pairs of scores go through one packed f32x2 FMA, then the
-            // hardware ex2; the row sum is kept in fp32 (four pair sums).
+            // of S. Pairs of scores go through one packed f32x2 FMA, then an
+            // exponent: three pairs in four on the MUFU unit, the fourth as a
+            // polynomial on the FMA pipe (relative error 1.5e-4, under the
+            // fp16 rounding of P), so both pipes share the work. The row sum
+            // is kept in fp32 (four pair sums).
             const std::uint64_t scale2 = pack_f32x2(p.scale_log2, p.scale_log2);
             const std::uint64_t neg_m2 = pack_f32x2(-m, -m);
             std::uint64_t sum2[4] = {0, 0, 0, 0};
@@ -533,8 +604,15 @@ __global__ void __launch_bounds__(kThreads, 1)
                 for (int e = 0; e < 16; ++e) {
                     const int i = c * 32 + e * 2;
                     const std::uint64_t x = ffma_f32x2(pack_u32x2(s[i], s[i + 1]), scale2, neg_m2);
-                    const float p0 = ex2_ftz(low_f32(x));
-                    const float p1 = ex2_ftz(high_f32(x));
+                    float p0, p1;
+                    if ((e & 3) == 3) {
+                        const std::uint64_t e2 = ex2_poly_f32x2(low_f32(x), high_f32(x));
+                        p0 = low_f32(e2);
+                        p1 = high_f32(e2);
+                    } else {
+                        p0 = ex2_ftz(low_f32(x));
+                        p1 = ex2_ftz(high_f32(x));
+                    }
                     sum2[e & 3] = fadd_f32x2(sum2[e & 3], pack_f32x2(p0, p1));
                     const __half2 h = __floats2half2_rn(p0, p1);
                     packed[e] = *reinterpret_cast<const std::uint32_t*>(&h);
@@ -547,7 +625,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             const std::uint64_t s0123 = fadd_f32x2(s01, s23);
             l += low_f32(s0123) + high_f32(s0123);
             tc_fence_before();
-            mbar_arrive(&bars[kBarP + t]);
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&bars[kBarP + t]);  // one arrival per warp
         }
         if (ok && warp_ok(wait(&bars[kBarO + t], (n - 1) & 1))) {
             tc_fence_after();
@@ -670,14 +749,11 @@ inline void run_tc_prefill(InferlabCudaKvPool& pool, const void* queries, std::u
     const cuuint64_t q_strides[2] = {kD * 2, static_cast<cuuint64_t>(q_heads) * kD * 2};
     const cuuint32_t q_box[3] = {64, 1, kBM};  // one 128-query tile per box
     const CUtensorMap q_map = make_map(q16, type, 3, q_dims, q_strides, q_box);
-    const cuuint64_t kv_dims[4] = {kD, kBlockTokens, pool.kv_heads, pool.num_blocks};
-    const cuuint64_t kv_strides[3] = {kD * 2, kBlockTokens * kD * 2,
-                                      static_cast<cuuint64_t>(pool.kv_heads) * kBlockTokens * kD * 2};
-    const cuuint32_t kv_box[4] = {64, kBlockTokens, 1, 1};
-    const CUtensorMap k_map = make_map(pool.key_arena, type, 4, kv_dims, kv_strides, kv_box);
-    const CUtensorMap v_map = make_map(pool.value_arena, type, 4, kv_dims, kv_strides, kv_box);
 
     Params params{};
+    params.key_arena = static_cast<const unsigned char*>(pool.key_arena);
+    params.value_arena = static_cast<const unsigned char*>(pool.value_arena);
+    params.kv_heads = pool.kv_heads;
     params.tables = tables;
     params.max_blocks = max_blocks;
     params.starts = starts;
@@ -697,7 +773,7 @@ inline void run_tc_prefill(InferlabCudaKvPool& pool, const void* queries, std::u
     auto kernel = bf16 ? prefill_tc_kernel<true> : prefill_tc_kernel<false>;
     cuda_check(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemAlloc),
                "cudaFuncSetAttribute");
-    kernel<<<static_cast<unsigned>(grid), kThreads, kSmemAlloc, stream>>>(q_map, k_map, v_map,
+    kernel<<<static_cast<unsigned>(grid), kThreads, kSmemAlloc, stream>>>(q_map,
                                                                           params);
     cuda_check(cudaGetLastError(), "tensor-core prefill launch");
 }
