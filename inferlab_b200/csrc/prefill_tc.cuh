@@ -155,6 +155,28 @@ __device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, i
         : "memory");
 }
 
+// Tensor store from shared memory (bulk async group) and its completion waits.
+__device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, const void* src, int c0, int c1,
+                                             int c2) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%1, %2, %3}], [%4];" ::"l"(
+            reinterpret_cast<std::uint64_t>(map)),
+        "r"(c0), "r"(c1), "r"(c2), "r"(smem_u32(src))
+        : "memory");
+}
+__device__ __forceinline__ void bulk_commit_group() {
+    asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+__device__ __forceinline__ void bulk_wait_group_read0() {
+    asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
+__device__ __forceinline__ void bulk_wait_group0() {
+    asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+}
+__device__ __forceinline__ void named_barrier_sync(int id, int count) {
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+
 // 32 consecutive TMEM columns of this thread's lane (32x32b shape).
 __device__ __forceinline__ void tmem_load32(std::uint32_t taddr, float* out) {
     std::uint32_t r[32];
@@ -252,6 +274,20 @@ __host__ __device__ constexpr std::uint32_t idesc_f16(std::uint32_t a_type, std:
 // (tcgen05.ld .sync.aligned) without the others.
 __device__ __forceinline__ bool warp_ok(bool ok) { return __all_sync(0xffffffffu, ok); }
 
+// Named barrier `id` over `count` threads that also ANDs a predicate across them.
+__device__ __forceinline__ bool named_barrier_and(int id, int count, bool pred) {
+    std::uint32_t r;
+    asm volatile(
+        "{\n\t.reg .pred p, q;\n\t"
+        "setp.ne.u32 p, %1, 0;\n\t"
+        "bar.red.and.pred q, %2, %3, p;\n\t"
+        "selp.u32 %0, 1, 0, q;\n\t}"
+        : "=r"(r)
+        : "r"(pred ? 1u : 0u), "r"(id), "r"(count)
+        : "memory");
+    return r != 0;
+}
+
 struct Waiter {
     int* abort;
     std::uint32_t* error_word;
@@ -270,7 +306,8 @@ struct Waiter {
 
 template <bool kBf16>
 __global__ void __launch_bounds__(kThreads, 1)
-    prefill_tc_kernel(const __grid_constant__ CUtensorMap q_map, const Params p) {
+    prefill_tc_kernel(const __grid_constant__ CUtensorMap q_map,
+                      const __grid_constant__ CUtensorMap out_map, const Params p) {
     extern __shared__ unsigned char smem_raw[];
     unsigned char* smem = reinterpret_cast<unsigned char*>(
         (reinterpret_cast<std::uintptr_t>(smem_raw) + 1023) & ~static_cast<std::uintptr_t>(1023));
@@ -628,27 +665,70 @@ __global__ void __launch_bounds__(kThreads, 1)
             __syncwarp();
             if (lane == 0) mbar_arrive(&bars[kBarP + t]);  // one arrival per warp
         }
-        if (ok && warp_ok(wait(&bars[kBarO + t], (n - 1) & 1))) {
-            tc_fence_after();
-            const float inv = 1.0f / l;
-            // Every lane takes part in the TMEM loads (warp-collective); only
-            // rows inside the segment store.
-            const bool store = row < rows[t];
-            float* out = p.out + (static_cast<std::size_t>(offset + q_lo + t * kBM + (store ? row : 0)) *
-                                      p.q_heads + head) * kD;
+        if (n > 0) {
+            const bool done = ok && warp_ok(wait(&bars[kBarO + t], (n - 1) & 1));
+            // The tile's four warps agree (named barrier) before any of them
+            // takes part in the shared staging below.
+            const bool all_done = named_barrier_and(1 + t, kBM, done);
+            if (all_done) {
+                tc_fence_after();
+                const float inv = 1.0f / l;
+                if (rows[t] == kBM) {
+                    // Full tile: O / l through shared memory and tensor stores,
+                    // 64 columns at a time in the tile's Q buffer (no MMA reads
+                    // it any more): two 128-row x 32-float boxes, 128-byte
+                    // swizzled (row r's 16-byte chunk c at r * 128 +
+                    // 16 (c ^ (r & 7))), so the staging writes are free of bank
+                    // conflicts and the global writes are whole lines.
+                    unsigned char* stage = smem + kQ0 + t * kTile;
+                    const int q_row = offset + q_lo + t * kBM;
+#pragma unroll 1
+                    for (int hb = 0; hb < 2; ++hb) {
 #pragma unroll
-            for (int c = 0; c < 4; ++c) {
-                float o[32];
-                tmem_load32(lane_addr + 128 + c * 32, o);
-                if (store) {
+                        for (int b = 0; b < 2; ++b) {
+                            float o[32];
+                            tmem_load32(lane_addr + 128 + (hb * 2 + b) * 32, o);
+                            unsigned char* box = stage + b * kHalf + row * 128;
 #pragma unroll
-                    for (int i = 0; i < 32; i += 4) {
-                        *reinterpret_cast<float4*>(out + c * 32 + i) =
-                            make_float4(o[i] * inv, o[i + 1] * inv, o[i + 2] * inv, o[i + 3] * inv);
+                            for (int cch = 0; cch < 8; ++cch) {
+                                *reinterpret_cast<float4*>(box + ((cch ^ (row & 7)) << 4)) =
+                                    make_float4(o[4 * cch] * inv, o[4 * cch + 1] * inv,
+                                                o[4 * cch + 2] * inv, o[4 * cch + 3] * inv);
+                            }
+                        }
+                        fence_proxy_async_shared();
+                        named_barrier_sync(1 + t, kBM);
+                        if (row == 0) {
+                            tma_store_3d(&out_map, stage, (hb * 2) * 32, static_cast<int>(head), q_row);
+                            tma_store_3d(&out_map, stage + kHalf, (hb * 2 + 1) * 32, static_cast<int>(head),
+                                         q_row);
+                            bulk_commit_group();
+                            bulk_wait_group_read0();  // staging may be overwritten
+                        }
+                        named_barrier_sync(1 + t, kBM);
+                    }
+                    if (row == 0) bulk_wait_group0();
+                } else {
+                    // Ragged last tile of a segment: rows past its end belong
+                    // to the next segment, so only rows inside it store.
+                    const bool store = row < rows[t];
+                    float* out = p.out + (static_cast<std::size_t>(offset + q_lo + t * kBM + (store ? row : 0)) *
+                                              p.q_heads + head) * kD;
+#pragma unroll
+                    for (int c = 0; c < 4; ++c) {
+                        float o[32];
+                        tmem_load32(lane_addr + 128 + c * 32, o);
+                        if (store) {
+#pragma unroll
+                            for (int i = 0; i < 32; i += 4) {
+                                *reinterpret_cast<float4*>(out + c * 32 + i) =
+                                    make_float4(o[i] * inv, o[i + 1] * inv, o[i + 2] * inv, o[i + 3] * inv);
+                            }
+                        }
                     }
                 }
+                if (row < rows[t] && !(isfinite(l) && l > 0.0f)) flag_error(p.error_word, kErrNormalizer);
             }
-            if (store && !(isfinite(l) && l > 0.0f)) flag_error(p.error_word, kErrNormalizer);
         }
     }
     tc_fence_before();
@@ -749,6 +829,13 @@ inline void run_tc_prefill(InferlabCudaKvPool& pool, const void* queries, std::u
     const cuuint64_t q_strides[2] = {kD * 2, static_cast<cuuint64_t>(q_heads) * kD * 2};
     const cuuint32_t q_box[3] = {64, 1, kBM};  // one 128-query tile per box
     const CUtensorMap q_map = make_map(q16, type, 3, q_dims, q_strides, q_box);
+    if (reinterpret_cast<std::uintptr_t>(out) % 16 != 0) {
+        throw std::runtime_error("paged prefill output must be 16-byte aligned");
+    }
+    const cuuint64_t o_dims[3] = {kD, q_heads, static_cast<cuuint64_t>(total_queries)};
+    const cuuint64_t o_strides[2] = {kD * 4, static_cast<cuuint64_t>(q_heads) * kD * 4};
+    const cuuint32_t o_box[3] = {32, 1, kBM};  // 128 rows x 32 floats (128 B)
+    const CUtensorMap out_map = make_map(out, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, o_dims, o_strides, o_box);
 
     Params params{};
     params.key_arena = static_cast<const unsigned char*>(pool.key_arena);
@@ -773,7 +860,7 @@ inline void run_tc_prefill(InferlabCudaKvPool& pool, const void* queries, std::u
     auto kernel = bf16 ? prefill_tc_kernel<true> : prefill_tc_kernel<false>;
     cuda_check(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemAlloc),
                "cudaFuncSetAttribute");
-    kernel<<<static_cast<unsigned>(grid), kThreads, kSmemAlloc, stream>>>(q_map,
+    kernel<<<static_cast<unsigned>(grid), kThreads, kSmemAlloc, stream>>>(q_map, out_map,
                                                                           params);
     cuda_check(cudaGetLastError(), "tensor-core prefill launch");
 }
