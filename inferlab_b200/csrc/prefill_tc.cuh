@@ -318,10 +318,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
 
-    // Work item, heaviest (last) query blocks first.
-    const std::uint32_t qblk = p.q_blocks - 1 - blockIdx.x % p.q_blocks;
-    const std::uint32_t head = (blockIdx.x / p.q_blocks) % p.q_heads;
-    const std::uint32_t seg = blockIdx.x / (p.q_blocks * p.q_heads);
+    // Work item: all (segment, head) pairs of the last query block first, then
+    // the block before it, ... - longest causal work first, so the short
+    // blocks fill the tail of the grid.
+    const std::uint32_t pairs = p.num_segments * p.q_heads;
+    const std::uint32_t qblk = p.q_blocks - 1 - blockIdx.x / pairs;
+    const std::uint32_t head = (blockIdx.x % pairs) % p.q_heads;
+    const std::uint32_t seg = (blockIdx.x % pairs) / p.q_heads;
     const int count = p.counts[seg];
     const int q_lo = static_cast<int>(qblk) * kQBlock;
     if (q_lo >= count) return;
