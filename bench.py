@@ -15,7 +15,12 @@ rank time ("scaling": "weak").
 
 Other workloads: longctx_bf16 (256 sequences, context U[4096, 32768], GQA
 32/8 x 128, bf16; sequences sharded across ranks, strong scaling), prefill_f16
-(8 x 1024 causal prefill, 16 heads x 128, f16; TFLOP/s).
+(8 x 1024 causal prefill, 16 heads x 128, f16; TFLOP/s), mixed_bf16 (one
+continuous-batching step), longseq_split (one 131,072-token sequence split
+across ranks, NCCL merge), single_seq_fp32 (the drop-in C entry
+inferlab_attention_forward with host buffers on one 129 x 4 x 32 sequence:
+prefill of 128 queries plus one decode query; launch-bound, microseconds per
+call, no roofline claim).
 
 --impl reference times the reference's own CPU kernel
 (oracle/_ref/libref.so, compiled from kernels/attention_cpu.cpp) on the same
@@ -246,6 +251,8 @@ def run_ours(args):
         return run_prefill(args, dist, world, rank, device, peaks, peak_kind)
     if args.workload == "mixed_bf16":
         return run_mixed(args, dist, world, rank, device, peaks, peak_kind)
+    if args.workload == "single_seq_fp32":
+        return run_single_sequence(args, dist, world, rank, device)
     if args.workload == "longseq_split":
         return run_long_sequence(args, dist, world, rank, device, peaks, peak_kind)
 
@@ -402,6 +409,80 @@ def host_threads() -> int:
         return os.cpu_count() or 1
 
 
+def cpu_model() -> str:
+    try:
+        with open("/proc/cpuinfo") as handle:
+            for line in handle:
+                if line.startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+def run_single_sequence(args, dist, world, rank, device):
+    """The reference's own CPU-runnable case through the drop-in C entry:
+    Q/K/V ~ N(0, 1) [129][4][32] fp32; prefill of the first 128 queries
+    (start 0, causal, OnlineTiled tile 16) and decode of query 128 against all
+    129 keys (start 128). A step is both calls, host buffers in and out (each
+    call copies its inputs to the device, runs one kernel and copies the
+    output back). Timed on the host clock around each call pair; the reference
+    CPU kernel (oracle/_ref/libref.so) runs the same calls for cpu_baseline."""
+    import inferlab_b200 as il
+    from oracle import oracle
+
+    rng = np.random.Generator(np.random.PCG64(20261201))
+    t, h, d = 129, 4, 32
+    q = rng.standard_normal(t * h * d, dtype=np.float32)
+    k = rng.standard_normal(t * h * d, dtype=np.float32)
+    v = rng.standard_normal(t * h * d, dtype=np.float32)
+    cfg = il.AttentionConfig(il.AttentionAlgorithm.ONLINE_TILED)
+    width = h * d
+
+    def ours():
+        il.run_attention(q[:128 * width], k[:128 * width], v[:128 * width], 128, 128, h, d, 0, cfg)
+        il.run_attention(q[128 * width:], k, v, 1, 129, h, d, 128, cfg)
+
+    def reference():
+        oracle.attention_forward(q[:128 * width], k[:128 * width], v[:128 * width], 128, 128, h,
+                                 d, 0, oracle.ONLINE_TILED, oracle.FP32, 16, impl="reference")
+        oracle.attention_forward(q[128 * width:], k, v, 1, 129, h, d, 128, oracle.ONLINE_TILED,
+                                 oracle.FP32, 16, impl="reference")
+
+    for _ in range(args.warmup):
+        ours()
+    times = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        ours()
+        times.append(time.perf_counter() - t0)
+    us = statistics.median(times) * 1e6
+    line = {
+        "metric": "drop-in attention_forward us per call pair", "value": round(us, 2),
+        "unit": "us", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(us / 1e3, 4), "higher_is_better": False, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded N(0,1))",
+        "config": {"workload": "single sequence 129 x 4 heads x 32, fp32: prefill 128 + decode 1 "
+                               "through inferlab_attention_forward (host buffers)",
+                   "timing": "host clock, median of steps; launch-bound, no roofline claim"},
+        "gpu_launches": 2 * args.steps,
+    }
+    if rank == 0 and not args.no_cpu_baseline and oracle.ref_lib() is not None:
+        for _ in range(3):
+            reference()
+        ref_times = []
+        for _ in range(max(args.steps, 20)):
+            t0 = time.perf_counter()
+            reference()
+            ref_times.append(time.perf_counter() - t0)
+        line["cpu_baseline"] = {"value": round(statistics.median(ref_times) * 1e6, 2), "unit": "us",
+                                "cores": 1, "kind": "reference", "cpu_model": cpu_model(),
+                                "sample": "the same two calls on oracle/_ref/libref.so "
+                                          "(kernels/attention_cpu.cpp), one thread"}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
 def cpu_baseline_decode(batch, bytes_per_step, seconds: float) -> dict:
     """The reference CPU kernel on the same pool contents, all host threads."""
     from inferlab_b200 import workloads as wl
@@ -421,8 +502,14 @@ def cpu_baseline_decode(batch, bytes_per_step, seconds: float) -> dict:
         if elapsed >= seconds:
             break
     kind = "reference" if oracle.ref_lib() is not None else "port"
+    # single-thread rate on one pass of the same batch
+    t1 = time.perf_counter()
+    oracle.reference_paged_decode_timed(k_host, v_host, batch.pool.dtype, batch.tables_host,
+                                        batch.contexts, q, batch.q_heads, 1)
+    single = bytes_per_step / (time.perf_counter() - t1) / 1e9
     return {"value": round(bytes_per_step * steps / elapsed / 1e9, 4), "unit": "GB/s",
-            "cores": threads, "kind": kind,
+            "cores": threads, "kind": kind, "cpu_model": cpu_model(),
+            "single_thread_value": round(single, 4),
             "sample": f"{steps} full steps ({sample} sequences each) in {elapsed:.1f} s: page gather "
                       "+ inferlab_attention_forward (OnlineTiled, tile 16) per q-head, "
                       "oracle/_ref/libref.so built from kernels/attention_cpu.cpp"}
@@ -708,7 +795,7 @@ def main():
     parser.add_argument("--impl", choices=["ours", "reference"], default="ours")
     parser.add_argument("--workload", default="decode_fp32",
                         choices=["decode_fp32", "longctx_bf16", "prefill_f16", "mixed_bf16",
-                                 "longseq_split"])
+                                 "longseq_split", "single_seq_fp32"])
     parser.add_argument("--cpu-seconds", type=float, default=10.0)
     parser.add_argument("--no-cpu-baseline", action="store_true")
     args = parser.parse_args()
