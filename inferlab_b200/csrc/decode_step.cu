@@ -59,6 +59,17 @@ StepLayout layout_for(const InferlabCudaKvPool& p, std::uint32_t num_seqs, std::
 }
 
 // Grow-only pinned + device staging (one allocation each, reused across steps).
+// Page-locked host memory (cudaHostAlloc / cudaHostRegister): the DMA engine
+// can read and write it directly, so the step skips the staging memcpy.
+bool is_pinned(const void* ptr) {
+    cudaPointerAttributes attr{};
+    if (cudaPointerGetAttributes(&attr, ptr) != cudaSuccess) {
+        cudaGetLastError();  // pageable memory on old runtimes reports an error; clear it
+        return false;
+    }
+    return attr.type == cudaMemoryTypeHost;
+}
+
 void reserve_step(InferlabCudaKvPool& p, std::size_t bytes, cudaStream_t stream) {
     if (bytes <= p.step_capacity) return;
     wait_stream(stream, 0);  // no step may still be using the old buffers
@@ -125,23 +136,46 @@ extern "C" int inferlab_cuda_decode_step_host(
         unsigned char* h = p.step_host;
         unsigned char* d = p.step_device;
         const std::size_t q_bytes = static_cast<std::size_t>(num_seqs) * q_heads * p.head_dim * 4;
-        std::memcpy(h + l.q, queries, q_bytes);
-        if (append) {
-            const std::size_t row_bytes = static_cast<std::size_t>(num_seqs) * p.kv_heads * p.head_dim * 4;
-            std::memcpy(h + l.k, new_keys, row_bytes);
-            std::memcpy(h + l.v, new_values, row_bytes);
-        }
-        std::memcpy(h + l.tables, block_tables,
-                    static_cast<std::size_t>(num_seqs) * max_blocks_per_seq * 4);
-        std::memcpy(h + l.lens, context_lens, static_cast<std::size_t>(num_seqs) * 4);
+        const std::size_t row_bytes = static_cast<std::size_t>(num_seqs) * p.kv_heads * p.head_dim * 4;
+        const std::size_t table_bytes = static_cast<std::size_t>(num_seqs) * max_blocks_per_seq * 4;
+        // Caller buffers already page-locked: copy them straight to HBM (and
+        // the output straight back) instead of through the staging buffer.
+        const bool direct = is_pinned(queries) && is_pinned(block_tables) &&
+                            is_pinned(context_lens) && is_pinned(out) &&
+                            (!append || (is_pinned(new_keys) && is_pinned(new_values)));
         auto* pos = reinterpret_cast<std::int32_t*>(h + l.pos);
         auto* seq = reinterpret_cast<std::int32_t*>(h + l.seq);
         for (std::uint32_t i = 0; i < num_seqs; ++i) {
             pos[i] = context_lens[i] - 1;  // the new token sits at the last position
             seq[i] = static_cast<std::int32_t>(i);
         }
-        cuda_check(cudaMemcpyAsync(d, h, l.inputs_end, cudaMemcpyHostToDevice, s),
-                   "cudaMemcpyAsync step inputs");
+        if (direct) {
+            cuda_check(cudaMemcpyAsync(d + l.pos, h + l.pos, l.inputs_end - l.pos, cudaMemcpyHostToDevice, s),
+                       "cudaMemcpyAsync step positions");
+            cuda_check(cudaMemcpyAsync(d + l.tables, block_tables, table_bytes, cudaMemcpyHostToDevice, s),
+                       "cudaMemcpyAsync step tables");
+            cuda_check(cudaMemcpyAsync(d + l.lens, context_lens, static_cast<std::size_t>(num_seqs) * 4,
+                                       cudaMemcpyHostToDevice, s),
+                       "cudaMemcpyAsync step lengths");
+            if (append) {
+                cuda_check(cudaMemcpyAsync(d + l.k, new_keys, row_bytes, cudaMemcpyHostToDevice, s),
+                           "cudaMemcpyAsync step keys");
+                cuda_check(cudaMemcpyAsync(d + l.v, new_values, row_bytes, cudaMemcpyHostToDevice, s),
+                           "cudaMemcpyAsync step values");
+            }
+            cuda_check(cudaMemcpyAsync(d + l.q, queries, q_bytes, cudaMemcpyHostToDevice, s),
+                       "cudaMemcpyAsync step queries");
+        } else {
+            std::memcpy(h + l.q, queries, q_bytes);
+            if (append) {
+                std::memcpy(h + l.k, new_keys, row_bytes);
+                std::memcpy(h + l.v, new_values, row_bytes);
+            }
+            std::memcpy(h + l.tables, block_tables, table_bytes);
+            std::memcpy(h + l.lens, context_lens, static_cast<std::size_t>(num_seqs) * 4);
+            cuda_check(cudaMemcpyAsync(d, h, l.inputs_end, cudaMemcpyHostToDevice, s),
+                       "cudaMemcpyAsync step inputs");
+        }
         // The split counters at the front of the workspace start at zero.
         cuda_check(cudaMemsetAsync(d + l.workspace, 0, decode_counter_bytes(p, num_seqs), s),
                    "cudaMemsetAsync step workspace");
@@ -158,9 +192,16 @@ extern "C" int inferlab_cuda_decode_step_host(
                             d + l.workspace, p.step_capacity - l.workspace, s);
         cuda_check(cudaMemcpyAsync(d + l.err, p.error_word, 4, cudaMemcpyDeviceToDevice, s),
                    "cudaMemcpyAsync error word");
-        cuda_check(cudaMemcpyAsync(h + l.err, d + l.err, l.out + q_bytes - l.err,
-                                   cudaMemcpyDeviceToHost, s),
-                   "cudaMemcpyAsync step output");
+        if (direct) {
+            cuda_check(cudaMemcpyAsync(h + l.err, d + l.err, 4, cudaMemcpyDeviceToHost, s),
+                       "cudaMemcpyAsync step error word");
+            cuda_check(cudaMemcpyAsync(out, d + l.out, q_bytes, cudaMemcpyDeviceToHost, s),
+                       "cudaMemcpyAsync step output");
+        } else {
+            cuda_check(cudaMemcpyAsync(h + l.err, d + l.err, l.out + q_bytes - l.err,
+                                       cudaMemcpyDeviceToHost, s),
+                       "cudaMemcpyAsync step output");
+        }
         wait_stream(s, timeout_ms);
         std::uint32_t bits = 0;
         std::memcpy(&bits, h + l.err, 4);
@@ -169,6 +210,6 @@ extern "C" int inferlab_cuda_decode_step_host(
             wait_stream(s, timeout_ms);
             throw std::runtime_error(describe_error_bits(bits));
         }
-        std::memcpy(out, h + l.out, q_bytes);
+        if (!direct) std::memcpy(out, h + l.out, q_bytes);
     });
 }

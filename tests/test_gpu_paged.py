@@ -170,6 +170,39 @@ def test_decode_step_host_matches_device_calls(torch_mod, wl, oracle_mod):
     batch.pool.close()
 
 
+def test_decode_step_host_pinned_buffers_match_staged(torch_mod, wl):
+    """Page-locked caller buffers take the direct-DMA path; the result equals
+    the staged path on pageable copies of the same arrays, bit for bit."""
+    torch = torch_mod
+    contexts = np.array([5, 300, 1024, 77])
+    rng = np.random.Generator(np.random.PCG64(28))
+    q = rng.standard_normal((len(contexts), 16, 64), dtype=np.float32)
+    k_new = rng.standard_normal((len(contexts), 4, 64), dtype=np.float32)
+    v_new = rng.standard_normal((len(contexts), 4, 64), dtype=np.float32)
+
+    def pinned(a):
+        t = torch.empty(a.shape, dtype=getattr(torch, str(a.dtype)), pin_memory=True)
+        t.numpy()[...] = a
+        return t.numpy()
+
+    results = []
+    for use_pinned in (False, True):
+        batch = wl.decode_batch(0, 27, len(contexts), contexts, 16, 4, 64, wl.KV_FP32,
+                                max_context_len=1024)
+        tables = np.ascontiguousarray(batch.tables_host, dtype=np.int32)
+        lens = contexts.astype(np.int32)
+        args = (q, tables, lens, k_new, v_new)
+        if use_pinned:
+            args = tuple(pinned(a) for a in args)
+            out = pinned(np.zeros_like(q))
+        else:
+            out = np.zeros_like(q)
+        got = batch.pool.decode_step_host(args[0], args[1], args[2], args[3], args[4], out=out)
+        results.append(np.array(got))
+        batch.pool.close()
+    assert np.array_equal(results[0], results[1])
+
+
 def test_append_then_gather_bit_exact(torch_mod, wl, oracle_mod):
     torch = torch_mod
     from inferlab_b200 import CudaKvPool
