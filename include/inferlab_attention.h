@@ -299,6 +299,107 @@ int inferlab_cuda_paged_prefill(InferlabCudaKvPool* pool, const void* queries, u
                                 uint64_t total_queries, float* out, void* stream, char* error,
                                 size_t error_capacity);
 
+/* ---- Block ownership (host metadata over the device pool) -------------------
+ *
+ * The ownership model of the reference's PagedKvPool
+ * (worker/cpp/inferlab_runtime.cpp:649-1032) without its page storage, which
+ * lives in the device pool: a free list, reference counts, published prefixes
+ * with longest-prefix lookup and least-recently-used eviction, copy on write
+ * for a shared tail block, and InferlabPagedCacheStats. Block ids are the
+ * device pool's. All calls are host-only except inferlab_cuda_pages_copy.
+ */
+#ifndef INFERLAB_PAGED_CACHE_STATS_DEFINED
+#define INFERLAB_PAGED_CACHE_STATS_DEFINED
+/* Same layout and meaning as worker/cpp/inferlab_runtime.h:7-31. */
+typedef struct InferlabPagedCacheStats {
+    uint64_t page_tokens;
+    uint64_t page_count;
+    uint64_t prefix_capacity;
+    uint64_t page_bytes;
+    uint64_t capacity_bytes;
+    uint64_t allocated_pages;
+    uint64_t free_pages;
+    uint64_t used_token_slots;
+    uint64_t allocated_token_slots;
+    uint64_t internal_fragmentation_bytes;
+    uint64_t live_references;
+    uint64_t shared_pages;
+    uint64_t maximum_refcount;
+    uint64_t logical_referenced_bytes;
+    uint64_t physical_used_bytes;
+    uint64_t bytes_saved_by_sharing;
+    uint64_t prefix_entries;
+    uint64_t prefix_hits;
+    uint64_t prefix_misses;
+    uint64_t prefix_tokens_reused;
+    uint64_t copy_on_write_copies;
+    uint64_t evictions;
+    uint64_t allocation_failures;
+} InferlabPagedCacheStats;
+#endif
+
+typedef struct InferlabCudaPageManager InferlabCudaPageManager;
+
+/*
+ * A manager of page_count blocks of block_tokens token rows; row_bytes is one
+ * token row of K and V over all kv-heads (kv_heads * head_dim * 2 * element
+ * bytes), so page_bytes = block_tokens * row_bytes. Replaces PagedKvPool's
+ * constructor (:656-677; "paged KV cache dimensions must be positive").
+ */
+int inferlab_cuda_pages_create(uint64_t page_count, uint32_t block_tokens, uint64_t row_bytes,
+                               uint64_t prefix_capacity, InferlabCudaPageManager** manager,
+                               char* error, size_t error_capacity);
+void inferlab_cuda_pages_destroy(InferlabCudaPageManager* manager);
+
+/*
+ * Reserves the slot of token `cached_tokens` of a sequence whose block table
+ * is table[0 .. *table_length) (ceil(cached_tokens / block_tokens) entries,
+ * room for table_capacity): a new block when the slot starts one, else the
+ * tail block, copied first when it is shared - *copy_from / *copy_to name the
+ * blocks the caller copies on the device (inferlab_cuda_pages_copy) before it
+ * writes the row; both are -1 when no copy is needed. The allocation policy of
+ * PagedKvPool::append (:710-767), whose row write is inferlab_cuda_kv_append.
+ */
+int inferlab_cuda_pages_prepare_append(InferlabCudaPageManager* manager, int32_t* table,
+                                       uint32_t table_capacity, uint32_t* table_length,
+                                       uint64_t cached_tokens, int32_t* copy_from,
+                                       int32_t* copy_to, char* error, size_t error_capacity);
+
+/* Drops one reference on each block of the table (PagedKvPool::release_table, :848-855). */
+int inferlab_cuda_pages_release(InferlabCudaPageManager* manager, const int32_t* table,
+                                uint32_t length, char* error, size_t error_capacity);
+
+/* PagedKvPool::publish_prefix (:805-846): the first ceil(token_count / block_tokens) blocks. */
+int inferlab_cuda_pages_publish_prefix(InferlabCudaPageManager* manager, const uint32_t* tokens,
+                                       uint64_t token_count, const int32_t* table, uint32_t length,
+                                       uint64_t cached_tokens, char* error, size_t error_capacity);
+
+/*
+ * PagedKvPool::acquire_longest_prefix (:679-708): the longest published prefix
+ * of tokens, its blocks retained for the caller and written to table;
+ * *prefix_tokens = 0 and *table_length = 0 on a miss.
+ */
+int inferlab_cuda_pages_acquire_prefix(InferlabCudaPageManager* manager, const uint32_t* tokens,
+                                       uint64_t token_count, int32_t* table,
+                                       uint32_t table_capacity, uint32_t* table_length,
+                                       uint64_t* prefix_tokens, char* error, size_t error_capacity);
+
+/* PagedKvPool::shared_pages (:857-867): blocks of the table with more than one reference. */
+int inferlab_cuda_pages_shared(InferlabCudaPageManager* manager, const int32_t* table,
+                               uint32_t length, uint64_t* shared, char* error,
+                               size_t error_capacity);
+
+/* PagedKvPool::stats (:877-911) with the device pool's block and row sizes. */
+int inferlab_cuda_pages_stats(InferlabCudaPageManager* manager, InferlabPagedCacheStats* stats,
+                              char* error, size_t error_capacity);
+
+/*
+ * Copies whole blocks from[i] -> to[i] (K and V arenas, all kv-heads) on
+ * `stream`: the data movement of the copy on write (:741-750).
+ */
+int inferlab_cuda_pages_copy(InferlabCudaKvPool* pool, const int32_t* from, const int32_t* to,
+                             uint32_t count, void* stream, char* error, size_t error_capacity);
+
 /* Library version string, e.g. "inferlab-b200 0.1 sm_100a". */
 const char* inferlab_cuda_version(void);
 

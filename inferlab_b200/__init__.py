@@ -4,7 +4,9 @@ Drop-in for the reference's kernels/attention_cpu + paged KV cache:
   * run_attention: the worker's attention facade (worker/src/lib.rs:743-819)
     over the C entry inferlab_attention_forward, executed on the GPU;
   * CudaKvPool: the HBM block pool with append / gather / paged decode /
-    paged prefill kernels that follow the reference's block tables.
+    paged prefill kernels that follow the reference's block tables;
+  * PageManager: the block ownership model (reference counts, prefixes,
+    copy on write, eviction, InferlabPagedCacheStats) kept on the host.
 All compute is in libinferlab_attention_cuda.so (built by
 `python -m inferlab_b200.build`); importing this package does not need a GPU,
 calling it does.
@@ -15,6 +17,7 @@ from .attention import (AttentionAlgorithm, AttentionConfig, AttentionError,  # 
 __all__ = [
     "AttentionAlgorithm", "AttentionConfig", "AttentionError", "AttentionPrecision",
     "AttentionRun", "AttentionStats", "run_attention", "CudaKvPool", "lse_combine",
+    "PageManager",
 ]
 
 
@@ -24,4 +27,8 @@ def __getattr__(name):
         from . import paged
 
         return getattr(paged, name)
+    if name == "PageManager":
+        from . import pages
+
+        return pages.PageManager
     raise AttributeError(name)

@@ -65,6 +65,21 @@ class InferlabCudaPoolInfo(ctypes.Structure):
     ]
 
 
+class InferlabPagedCacheStats(ctypes.Structure):
+    """worker/cpp/inferlab_runtime.h:7-31."""
+
+    _fields_ = [(name, ctypes.c_uint64) for name in (
+        "page_tokens", "page_count", "prefix_capacity", "page_bytes", "capacity_bytes",
+        "allocated_pages", "free_pages", "used_token_slots", "allocated_token_slots",
+        "internal_fragmentation_bytes", "live_references", "shared_pages", "maximum_refcount",
+        "logical_referenced_bytes", "physical_used_bytes", "bytes_saved_by_sharing",
+        "prefix_entries", "prefix_hits", "prefix_misses", "prefix_tokens_reused",
+        "copy_on_write_copies", "evictions", "allocation_failures")]
+
+
+c_u32p = ctypes.POINTER(ctypes.c_uint32)
+c_u64p = ctypes.POINTER(ctypes.c_uint64)
+
 # name -> (restype, argtypes)
 SIGNATURES = {
     "inferlab_attention_forward": (ctypes.c_int, [
@@ -104,6 +119,23 @@ SIGNATURES = {
     "inferlab_cuda_paged_prefill": (ctypes.c_int, [
         c_vp, c_vp, ctypes.c_uint32, c_vp, ctypes.c_uint32, c_vp, c_vp, c_vp, ctypes.c_uint32,
         ctypes.c_uint32, ctypes.c_uint32, ctypes.c_uint64, c_vp, c_vp, c_err, c_sz]),
+    "inferlab_cuda_pages_create": (ctypes.c_int, [
+        ctypes.c_uint64, ctypes.c_uint32, ctypes.c_uint64, ctypes.c_uint64, ctypes.POINTER(c_vp),
+        c_err, c_sz]),
+    "inferlab_cuda_pages_destroy": (None, [c_vp]),
+    "inferlab_cuda_pages_prepare_append": (ctypes.c_int, [
+        c_vp, c_i32p, ctypes.c_uint32, c_u32p, ctypes.c_uint64, c_i32p, c_i32p, c_err, c_sz]),
+    "inferlab_cuda_pages_release": (ctypes.c_int, [c_vp, c_i32p, ctypes.c_uint32, c_err, c_sz]),
+    "inferlab_cuda_pages_publish_prefix": (ctypes.c_int, [
+        c_vp, c_u32p, ctypes.c_uint64, c_i32p, ctypes.c_uint32, ctypes.c_uint64, c_err, c_sz]),
+    "inferlab_cuda_pages_acquire_prefix": (ctypes.c_int, [
+        c_vp, c_u32p, ctypes.c_uint64, c_i32p, ctypes.c_uint32, c_u32p, c_u64p, c_err, c_sz]),
+    "inferlab_cuda_pages_shared": (ctypes.c_int, [
+        c_vp, c_i32p, ctypes.c_uint32, c_u64p, c_err, c_sz]),
+    "inferlab_cuda_pages_stats": (ctypes.c_int, [
+        c_vp, ctypes.POINTER(InferlabPagedCacheStats), c_err, c_sz]),
+    "inferlab_cuda_pages_copy": (ctypes.c_int, [
+        c_vp, c_i32p, c_i32p, ctypes.c_uint32, c_vp, c_err, c_sz]),
     "inferlab_cuda_version": (ctypes.c_char_p, []),
 }
 
