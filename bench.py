@@ -667,7 +667,7 @@ def run_mixed(args, dist, world, rank, device, peaks, peak_kind):
         "prefill": {"ms": round(ms_p / args.steps, 5),
                     "TFLOP/s": round(flops / (ms_p / args.steps) / 1e9, 2),
                     "frac_tensor": round(flops / (ms_p / args.steps) / 1e9 / peaks["bf16_tflops"], 4)},
-        "gpu_launches": 2 * args.steps, "clocks": clocks.summary(),
+        "gpu_launches": 3 * args.steps, "clocks": clocks.summary(),
     }
     pool.close()
     if rank == 0:
@@ -678,12 +678,12 @@ def run_mixed(args, dist, world, rank, device, peaks, peak_kind):
 
 def run_long_sequence(args, dist, world, rank, device, peaks, peak_kind):
     """One 131072-token sequence split across the ranks: per step, decode
-    partials over the local blocks, all-gather of (m, l, o) over NCCL, rank-order
-    log-sum-exp merge. Timed per rank with events, max over ranks."""
+    partials over the local blocks into one packed [m | l | o] block, one NCCL
+    all-gather of the blocks, rank-order log-sum-exp merge. Timed per rank with
+    events, max over ranks."""
     import torch
 
     from inferlab_b200 import distributed, workloads as wl
-    from inferlab_b200.paged import lse_combine
 
     batch = wl.long_sequence_shard(device, rank, world)
     pool = batch.pool
@@ -693,13 +693,10 @@ def run_long_sequence(args, dist, world, rank, device, peaks, peak_kind):
     workspace = pool.make_workspace(1, 32, local)
 
     def step():
-        m, l, o = pool.decode_partials(batch.queries, batch.block_tables, batch.context_lens,
-                                       local, workspace=workspace)
-        if dist is not None:
-            gm, gl, go = distributed.all_gather_partials(m, l, o)
-        else:
-            gm, gl, go = m[None], l[None], o[None]
-        return lse_combine(gm, gl, go)
+        # partials written as one packed [m | l | o] block, one NCCL all-gather,
+        # one rank-order merge kernel
+        return distributed.decode_split_sequence(pool, batch.queries, batch.block_tables, local,
+                                                 workspace=workspace)
 
     for i in range(args.warmup):
         flush.fill_(float(i))
@@ -722,7 +719,7 @@ def run_long_sequence(args, dist, world, rank, device, peaks, peak_kind):
         "roofline": {"bound": "hbm", "achieved_per_gpu": round(value / world, 2),
                      "peak": peaks["hbm_gbs"], "unit": "GB/s",
                      "frac": round(value / world / peaks["hbm_gbs"], 4)},
-        "gpu_launches": 2 * args.steps, "clocks": clocks.summary(),
+        "gpu_launches": 3 * args.steps, "clocks": clocks.summary(),
     }
     pool.close()
     if rank == 0:

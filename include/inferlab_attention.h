@@ -275,6 +275,17 @@ int inferlab_cuda_lse_combine(const float* part_m, const float* part_l, const fl
                               void* stream, char* error, size_t error_capacity);
 
 /*
+ * The same merge over `parts` packed partials, part i at
+ * packed + i * rows * (head_dim + 2) laid out as [m: rows][l: rows]
+ * [o: rows][head_dim] - one block per rank as a single all-gather of
+ * [m | l | o] delivers them (inferlab_cuda_paged_decode_partials can write the
+ * three pieces of the local block directly). No reference counterpart.
+ */
+int inferlab_cuda_lse_combine_packed(const float* packed, uint32_t parts, uint64_t rows,
+                                     uint32_t head_dim, float* out, void* stream, char* error,
+                                     size_t error_capacity);
+
+/*
  * Causal prefill / chunked prefill over the paged pool. Segment s has
  * query_counts[s] query tokens at positions [query_starts[s],
  * query_starts[s] + query_counts[s]) of its sequence, whose keys and values

@@ -116,6 +116,8 @@ SIGNATURES = {
     "inferlab_cuda_lse_combine": (ctypes.c_int, [
         c_vp, c_vp, c_vp, ctypes.c_uint32, ctypes.c_uint64, ctypes.c_uint32, c_vp, c_vp, c_err,
         c_sz]),
+    "inferlab_cuda_lse_combine_packed": (ctypes.c_int, [
+        c_vp, ctypes.c_uint32, ctypes.c_uint64, ctypes.c_uint32, c_vp, c_vp, c_err, c_sz]),
     "inferlab_cuda_paged_prefill": (ctypes.c_int, [
         c_vp, c_vp, ctypes.c_uint32, c_vp, ctypes.c_uint32, c_vp, c_vp, c_vp, ctypes.c_uint32,
         ctypes.c_uint32, ctypes.c_uint32, ctypes.c_uint64, c_vp, c_vp, c_err, c_sz]),

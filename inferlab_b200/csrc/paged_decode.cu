@@ -484,27 +484,31 @@ __global__ void __launch_bounds__(kDecodeWarps * 32)
 }
 
 // K4: log-sum-exp merge of partials in part order; one warp per row.
+// Part i of the merge reads m at part_m + i * stride_m, l at part_l +
+// i * stride_l and o at part_o + i * stride_o: dense [parts][rows] arrays, or
+// one packed [m | l | o] block per part as an all-gather delivers it.
 __global__ void lse_combine_kernel(const float* part_m, const float* part_l, const float* part_o,
                                    std::uint32_t parts, std::uint64_t rows, std::uint32_t head_dim,
-                                   float* out) {
+                                   std::uint64_t stride_m, std::uint64_t stride_l,
+                                   std::uint64_t stride_o, float* out) {
     const std::uint64_t row = static_cast<std::uint64_t>(blockIdx.x) * (blockDim.x / 32) +
                               threadIdx.x / 32;
     const int lane = threadIdx.x & 31;
     if (row >= rows) return;
     float mw = -INFINITY;
     for (std::uint32_t i = 0; i < parts; ++i) {
-        if (part_l[i * rows + row] > 0.0f) mw = fmaxf(mw, part_m[i * rows + row]);
+        if (part_l[i * stride_l + row] > 0.0f) mw = fmaxf(mw, part_m[i * stride_m + row]);
     }
     float lsum = 0.0f;
     for (std::uint32_t i = 0; i < parts; ++i) {
-        const float li = part_l[i * rows + row];
-        if (li > 0.0f) lsum += li * expf(part_m[i * rows + row] - mw);
+        const float li = part_l[i * stride_l + row];
+        if (li > 0.0f) lsum += li * expf(part_m[i * stride_m + row] - mw);
     }
     for (std::uint32_t dim = lane; dim < head_dim; dim += 32) {
         float a = 0.0f;
         for (std::uint32_t i = 0; i < parts; ++i) {
-            if (part_l[i * rows + row] > 0.0f) {
-                a += part_o[(i * rows + row) * head_dim + dim] * expf(part_m[i * rows + row] - mw);
+            if (part_l[i * stride_l + row] > 0.0f) {
+                a += part_o[i * stride_o + row * head_dim + dim] * expf(part_m[i * stride_m + row] - mw);
             }
         }
         out[row * head_dim + dim] = a / lsum;
@@ -833,6 +837,24 @@ extern "C" int inferlab_cuda_paged_decode_partials(
     });
 }
 
+namespace {
+
+void launch_lse_combine(const float* part_m, const float* part_l, const float* part_o,
+                        std::uint32_t parts, std::uint64_t rows, std::uint32_t head_dim,
+                        std::uint64_t stride_m, std::uint64_t stride_l, std::uint64_t stride_o,
+                        float* out, void* stream) {
+    if (parts == 0 || head_dim == 0) {
+        throw std::runtime_error("lse combine parts and head_dim must be positive");
+    }
+    const std::uint64_t blocks = (rows + 3) / 4;
+    if (blocks > 0x7FFFFFFFull) throw std::runtime_error("lse combine is too large");
+    ilb::lse_combine_kernel<<<static_cast<unsigned>(blocks), 128, 0, static_cast<cudaStream_t>(stream)>>>(
+        part_m, part_l, part_o, parts, rows, head_dim, stride_m, stride_l, stride_o, out);
+    ilb::cuda_check(cudaGetLastError(), "lse combine launch");
+}
+
+}  // namespace
+
 extern "C" int inferlab_cuda_lse_combine(const float* part_m, const float* part_l,
                                          const float* part_o, std::uint32_t parts,
                                          std::uint64_t rows, std::uint32_t head_dim, float* out,
@@ -842,14 +864,20 @@ extern "C" int inferlab_cuda_lse_combine(const float* part_m, const float* part_
         if (part_m == nullptr || part_l == nullptr || part_o == nullptr || out == nullptr) {
             throw std::runtime_error("lse combine pointer is null");
         }
-        if (parts == 0 || head_dim == 0) {
-            throw std::runtime_error("lse combine parts and head_dim must be positive");
-        }
-        const std::uint64_t blocks = (rows + 3) / 4;
-        if (blocks > 0x7FFFFFFFull) throw std::runtime_error("lse combine is too large");
-        ilb::lse_combine_kernel<<<static_cast<unsigned>(blocks), 128, 0,
-                                  static_cast<cudaStream_t>(stream)>>>(part_m, part_l, part_o,
-                                                                       parts, rows, head_dim, out);
-        ilb::cuda_check(cudaGetLastError(), "lse combine launch");
+        launch_lse_combine(part_m, part_l, part_o, parts, rows, head_dim, rows, rows,
+                           rows * head_dim, out, stream);
+    });
+}
+
+extern "C" int inferlab_cuda_lse_combine_packed(const float* packed, std::uint32_t parts,
+                                                std::uint64_t rows, std::uint32_t head_dim,
+                                                float* out, void* stream, char* error,
+                                                std::size_t error_capacity) {
+    return ilb::protect(error, error_capacity, [&] {
+        if (rows == 0) return;
+        if (packed == nullptr || out == nullptr) throw std::runtime_error("lse combine pointer is null");
+        const std::uint64_t part = rows * (static_cast<std::uint64_t>(head_dim) + 2);
+        launch_lse_combine(packed, packed + rows, packed + 2 * rows, parts, rows, head_dim, part,
+                           part, part, out, stream);
     });
 }

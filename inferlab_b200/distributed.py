@@ -71,18 +71,30 @@ def decode_split_sequence(pool, queries, block_table, local_len: int, group=None
     """Decode one query per row against a sequence whose blocks are spread
     over the ranks: this rank's blocks are `block_table` (device int32
     [rows, blocks]) covering `local_len` tokens. Returns the merged output
-    [rows, q_heads, head_dim] on every rank."""
+    [rows, q_heads, head_dim] on every rank.
+
+    The partials are written straight into one packed [m | l | o] block, the
+    blocks of all ranks are exchanged with a single all-gather (NCCL), and
+    one kernel merges them in rank order."""
     import torch
+    import torch.distributed as dist
 
-    from .paged import lse_combine
+    from .paged import lse_combine_packed
 
-    rows = queries.shape[0]
-    lens = torch.full((rows,), local_len, dtype=torch.int32, device=queries.device)
+    rows, q_heads, hd = queries.shape
+    nrows = rows * q_heads
+    world = dist.get_world_size(group) if dist.is_initialized() else 1
+    send = torch.empty(nrows * (hd + 2), dtype=torch.float32, device=queries.device)
     if local_len > 0:
-        m, l, o = pool.decode_partials(queries, block_table, lens, local_len, workspace=workspace)
+        lens = torch.full((rows,), local_len, dtype=torch.int32, device=queries.device)
+        pool.decode_partials(queries, block_table, lens, local_len, workspace=workspace,
+                             packed=send)
     else:
-        m = torch.full(queries.shape[:2], float("-inf"), device=queries.device)
-        l = torch.zeros(queries.shape[:2], device=queries.device)
-        o = torch.zeros_like(queries)
-    gm, gl, go = all_gather_partials(m, l, o, group)
-    return lse_combine(gm, gl, go)
+        send[:nrows].fill_(float("-inf"))
+        send[nrows:].zero_()
+    if world > 1:
+        recv = torch.empty(world * send.numel(), dtype=torch.float32, device=queries.device)
+        dist.all_gather_into_tensor(recv, send, group=group)
+    else:
+        recv = send
+    return lse_combine_packed(recv, world, nrows, hd).view(rows, q_heads, hd)

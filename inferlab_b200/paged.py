@@ -244,8 +244,12 @@ class CudaKvPool:
 
     def decode_partials(self, queries: torch.Tensor, block_tables: torch.Tensor,
                         context_lens: torch.Tensor, max_context_len: int | None = None,
-                        workspace: torch.Tensor | None = None, stream=None):
-        """Split-KV partials (m, l, o) over this pool's part of each context."""
+                        workspace: torch.Tensor | None = None, stream=None,
+                        packed: torch.Tensor | None = None):
+        """Split-KV partials (m, l, o) over this pool's part of each context.
+        With `packed` (fp32, rows * (head_dim + 2) elements, rows = num_seqs *
+        q_heads) they are written into it as [m | l | o], the layout
+        lse_combine_packed merges after an all-gather."""
         dev = self.device
         _require(queries, "queries", torch.float32, dev)
         _require(block_tables, "block_tables", torch.int32, dev)
@@ -253,9 +257,19 @@ class CudaKvPool:
         num_seqs, q_heads, hd = queries.shape
         if max_context_len is None:
             max_context_len = int(context_lens.max().item())
-        m = torch.empty((num_seqs, q_heads), dtype=torch.float32, device=f"cuda:{dev}")
-        l = torch.empty_like(m)
-        o = torch.empty_like(queries)
+        if packed is not None:
+            rows = num_seqs * q_heads
+            _require(packed, "packed", torch.float32, dev)
+            if packed.numel() != rows * (hd + 2):
+                raise AttentionError("packed partials buffer has the wrong size")
+            flat = packed.view(-1)
+            m = flat[:rows].view(num_seqs, q_heads)
+            l = flat[rows:2 * rows].view(num_seqs, q_heads)
+            o = flat[2 * rows:].view(num_seqs, q_heads, hd)
+        else:
+            m = torch.empty((num_seqs, q_heads), dtype=torch.float32, device=f"cuda:{dev}")
+            l = torch.empty_like(m)
+            o = torch.empty_like(queries)
         if workspace is None:
             workspace = self._cached_workspace(num_seqs, q_heads, max_context_len, stream)
         error = _lib.error_buffer()
@@ -312,4 +326,21 @@ def lse_combine(part_m: torch.Tensor, part_l: torch.Tensor, part_o: torch.Tensor
     _check(_lib.lib().inferlab_cuda_lse_combine(
         _vp(part_m), _vp(part_l), _vp(part_o), parts, rows, hd, _vp(out),
         _stream_handle(dev, stream), error, len(error)), error)
+    return out
+
+
+def lse_combine_packed(packed: torch.Tensor, parts: int, rows: int, head_dim: int,
+                       out: torch.Tensor | None = None, stream=None) -> torch.Tensor:
+    """Merge `parts` packed [m | l | o] partial blocks (part order) into
+    [rows][head_dim]."""
+    dev = packed.device.index
+    _require(packed, "packed", torch.float32, dev)
+    if packed.numel() != parts * rows * (head_dim + 2):
+        raise AttentionError("packed partials buffer has the wrong size")
+    if out is None:
+        out = torch.empty((rows, head_dim), dtype=torch.float32, device=packed.device)
+    error = _lib.error_buffer()
+    _check(_lib.lib().inferlab_cuda_lse_combine_packed(
+        _vp(packed), parts, rows, head_dim, _vp(out), _stream_handle(dev, stream), error,
+        len(error)), error)
     return out

@@ -122,6 +122,15 @@ def test_partials_and_combine_equal_whole_context(torch_mod, wl, oracle_mod):
         parts_l.append(l)
         parts_o.append(o)
     merged = lse_combine(torch.stack(parts_m), torch.stack(parts_l), torch.stack(parts_o))
+    # the packed layout (one [m | l | o] block per part, as an all-gather
+    # delivers it) merges to the same bits
+    from inferlab_b200.paged import lse_combine_packed
+
+    packed = torch.cat([torch.cat([pm.reshape(-1), pl.reshape(-1), po.reshape(-1)])
+                        for pm, pl, po in zip(parts_m, parts_l, parts_o)])
+    rows = parts_m[0].numel()
+    merged_packed = lse_combine_packed(packed, len(parts_m), rows, parts_o[0].shape[-1])
+    assert torch.equal(merged_packed.view_as(merged), merged)
     batch.pool.synchronize()
     close(merged[0].cpu().numpy(), whole[0].cpu().numpy(), atol=2e-6, rtol=2e-5)
     # the oracle's merge of the same partials agrees with the device merge
