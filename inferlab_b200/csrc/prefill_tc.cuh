@@ -1,9 +1,10 @@
 // prefill_tc.cuh - causal / chunked prefill on the sm_100a tensor cores.
 //
 // Work item: one CTA per (segment, q-head, 256-query block) = two 128-query
-// tiles A and B that share every K/V tile. The keys a query may see follow
-// legal_sources (kernels/attention_cpu.cpp:113-123): query i of a segment that
-// starts at position P sees keys [0, P + i].
+// tiles A and B that share every K/V tile; the grid runs the longest causal
+// blocks first. The keys a query may see follow legal_sources
+// (kernels/attention_cpu.cpp:113-123): query i of a segment that starts at
+// position P sees keys [0, P + i].
 //
 // Roles (384 threads):
 //   warps 0-3 / 4-7  softmax for tile A / B: thread t owns query row t. Per
@@ -16,8 +17,11 @@
 //              grows by more than 2^8, so probabilities relative to the kept
 //              max stay <= 256 (exact in fp16's range) and the result is the
 //              same online-softmax recurrence (kernels/attention_cpu.cpp:364-386).
-//              Before releasing P_t(j) the tile's warps check that V(j) and,
-//              when the tile continues, K(j + 1) are resident.
+//              At the start of step j the tile's warps also check that V(j)
+//              and, when the tile continues, K(j + 1) are resident, so the
+//              issuer needs no other wait than P. At the end a full tile's O / l
+//              leaves through its (then idle) Q buffer by tensor stores; a
+//              ragged last tile stores its rows directly.
 //   warp 8     both Q tiles by TMA (3-D map over [tokens][q_heads][128]), then
 //              the K tiles: per 128-key tile the eight 16-token blocks the
 //              table names, gathered with 16-byte cp.async into the 128-byte
@@ -145,16 +149,6 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, i
         "l"(reinterpret_cast<std::uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(smem_u32(bar))
         : "memory");
 }
-__device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, int c0, int c1,
-                                            int c2, int c3, std::uint64_t* bar) {
-    asm volatile(
-        "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, %5}], [%6];" ::
-            "r"(smem_u32(dst)),
-        "l"(reinterpret_cast<std::uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(c3),
-        "r"(smem_u32(bar))
-        : "memory");
-}
-
 // Tensor store from shared memory (bulk async group) and its completion waits.
 __device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, const void* src, int c0, int c1,
                                              int c2) {
