@@ -186,11 +186,11 @@ extern "C" int inferlab_cuda_pool_create(std::int32_t device, std::uint32_t dtyp
             cudaFree(owned->key_arena);
             cuda_check(second, "cudaMalloc value arena");
         }
-        cuda_check(cudaMalloc(&owned->error_word, 16), "cudaMalloc error word");
+        cuda_check(cudaMalloc(&owned->error_word, ilb::kPoolWordBytes), "cudaMalloc error word");
         cuda_check(cudaMallocHost(&owned->error_host, 16), "cudaMallocHost");
         cuda_check(cudaMemset(owned->key_arena, 0, owned->arena_bytes), "cudaMemset");
         cuda_check(cudaMemset(owned->value_arena, 0, owned->arena_bytes), "cudaMemset");
-        cuda_check(cudaMemset(owned->error_word, 0, 16), "cudaMemset");
+        cuda_check(cudaMemset(owned->error_word, 0, ilb::kPoolWordBytes), "cudaMemset");
         cuda_check(cudaDeviceSynchronize(), "cudaDeviceSynchronize");
         *pool = owned.release();
     });

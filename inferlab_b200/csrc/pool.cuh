@@ -4,6 +4,7 @@
 
 #include "common.cuh"
 
+#include <atomic>
 #include <mutex>
 
 struct InferlabCudaKvPool {
@@ -18,7 +19,7 @@ struct InferlabCudaKvPool {
     std::uint64_t arena_bytes = 0;
     void* key_arena = nullptr;
     void* value_arena = nullptr;
-    std::uint32_t* error_word = nullptr;       // device
+    std::uint32_t* error_word = nullptr;       // device: error word, then work-queue counters
     std::uint32_t* error_host = nullptr;       // pinned mirror
     std::mutex mutex;                          // guards error_host / error readback
     // Grow-only staging of the host-buffer step entry (decode_step.cu).
@@ -26,9 +27,18 @@ struct InferlabCudaKvPool {
     unsigned char* step_host = nullptr;        // pinned
     unsigned char* step_device = nullptr;
     std::size_t step_capacity = 0;
+    // Persistent prefill launches take their work-queue counter pair
+    // (next item, CTAs finished) round-robin from kSchedulerSlots pairs that
+    // follow the error word; each launch returns its pair to zero on exit.
+    std::atomic<std::uint32_t> scheduler_next{0};
 };
 
 namespace ilb {
+
+constexpr std::uint32_t kSchedulerSlots = 64;
+// Device words behind pool.error_word: the error word (16 bytes), then the
+// work-queue counter pairs.
+constexpr std::size_t kPoolWordBytes = 16 + kSchedulerSlots * 2 * sizeof(std::uint32_t);
 
 inline InferlabCudaKvPool& checked_pool(InferlabCudaKvPool* pool) {
     if (pool == nullptr) throw std::runtime_error("paged KV pool pointer is null");
