@@ -1,10 +1,13 @@
 // prefill_tc.cuh - causal / chunked prefill on the sm_100a tensor cores.
 //
-// Work item: one CTA per (segment, q-head, 256-query block) = two 128-query
-// tiles A and B that share every K/V tile; the grid runs the longest causal
-// blocks first. The keys a query may see follow legal_sources
-// (kernels/attention_cpu.cpp:113-123): query i of a segment that starts at
-// position P sees keys [0, P + i].
+// Work item: (segment, q-head, 256-query block) = two 128-query tiles A and B
+// that share every K/V tile. Persistent grid, one CTA per SM: items are
+// numbered longest causal block first and taken from a global counter, so
+// the CTAs that finish early take the short items at the end. A CTA starts
+// the next item's Q and K/V loads and its first S MMAs while the softmax
+// warps finish the current one. The keys a query may see follow
+// legal_sources (kernels/attention_cpu.cpp:113-123): query i of a segment
+// that starts at position P sees keys [0, P + i].
 //
 // Roles (384 threads):
 //   warps 0-3 / 4-7  softmax for tile A / B: thread t owns query row t. Per
@@ -17,12 +20,13 @@
 //              grows by more than 2^8, so probabilities relative to the kept
 //              max stay <= 256 (exact in fp16's range) and the result is the
 //              same online-softmax recurrence (kernels/attention_cpu.cpp:364-386).
-//              At the start of step j the tile's warps also check that V(j)
-//              and, when the tile continues, K(j + 1) are resident, so the
-//              issuer needs no other wait than P. At the end a full tile's O / l
-//              leaves through its (then idle) Q buffer by tensor stores; a
-//              ragged last tile stores its rows directly.
-//   warp 8     both Q tiles by TMA (3-D map over [tokens][q_heads][128]), then
+//              Before P_t(j) the tile's warps also check that V(j) and, when
+//              the tile continues, K(j + 1) are resident, so the issuer needs
+//              no other wait than P. At the end a full tile's O / l
+//              leaves through the tile's 16 KB staging box by tensor stores;
+//              a ragged last tile stores its rows directly.
+//   warp 8     takes the work items (counter -> shared-memory ring), loads
+//              both Q tiles by TMA (3-D map over [tokens][q_heads][128]), then
 //              the K tiles: per 128-key tile the eight 16-token blocks the
 //              table names, gathered with 16-byte cp.async into the 128-byte
 //              swizzled layout, block ids read one tile ahead.
@@ -672,16 +676,6 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int j = 0; ok && j < n; ++j) {
                 const std::uint32_t gj = g + static_cast<std::uint32_t>(j);
                 const std::uint32_t sj = ns + static_cast<std::uint32_t>(j);
-                // PV_t(j) reads V(j) and S_t(j + 1) reads K(j + 1): both must be
-                // resident before P_t(j) releases the issuer (which waits on P
-                // only). Checked while S_t(j) is still being computed; both
-                // copies were issued about a step earlier.
-                if (kBf16) {
-                    if (!(ok = warp_ok(wait(&bars[kBarVReady + (gj & 1)], (gj >> 1) & 1)))) break;
-                } else {
-                    if (!(ok = warp_ok(wait(&bars[kBarV + (gj & 1)], (gj >> 1) & 1)))) break;
-                }
-                if (j + 1 < n && !(ok = warp_ok(wait(&bars[kBarK + ((gj + 1) & 1)], ((gj + 1) >> 1) & 1)))) break;
                 if (!(ok = warp_ok(wait(&bars[kBarS + t], sj & 1)))) break;
                 tc_fence_after();
                 std::uint32_t s[128];
@@ -701,11 +695,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                 float mx4[4] = {__uint_as_float(s[0]), __uint_as_float(s[1]), __uint_as_float(s[2]),
                                 __uint_as_float(s[3])};
 #pragma unroll
-                for (int i = 4; i < 128; i += 8) {
-#pragma unroll
-                    for (int u = 0; u < 4; ++u) {
-                        mx4[u] = fmax3(mx4[u], __uint_as_float(s[i + 2 * u]), __uint_as_float(s[i + 2 * u + 1]));
-                    }
+                for (int i = 4; i < 128; i += 2) {
+                    mx4[(i >> 1) & 3] = fmax3(mx4[(i >> 1) & 3], __uint_as_float(s[i]), __uint_as_float(s[i + 1]));
                 }
                 const float mx = fmax3(mx4[0], mx4[1], fmaxf(mx4[2], mx4[3]));
                 const float m_seen = fmaxf(m, mx * p.scale_log2);
@@ -770,6 +761,16 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const std::uint64_t s23 = fadd_f32x2(sum2[2], sum2[3]);
                 const std::uint64_t s0123 = fadd_f32x2(s01, s23);
                 l += low_f32(s0123) + high_f32(s0123);
+                // PV_t(j) reads V(j) and S_t(j + 1) reads K(j + 1): both must be
+                // resident before P_t(j) releases the issuer (which waits on P
+                // only). Checked last, so that copies still in flight overlap
+                // this step's softmax.
+                if (kBf16) {
+                    if (!(ok = warp_ok(wait(&bars[kBarVReady + (gj & 1)], (gj >> 1) & 1)))) break;
+                } else {
+                    if (!(ok = warp_ok(wait(&bars[kBarV + (gj & 1)], (gj >> 1) & 1)))) break;
+                }
+                if (j + 1 < n && !(ok = warp_ok(wait(&bars[kBarK + ((gj + 1) & 1)], ((gj + 1) >> 1) & 1)))) break;
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&bars[kBarP + t]);  // one arrival per warp
