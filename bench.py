@@ -355,9 +355,10 @@ def run_decode_e2e(args, batch, pool, workspace, flush, device, dist, bytes_per_
     """The same decode step through the C ABI with HOST buffers: one
     inferlab_cuda_decode_step_host call per step takes the step's queries,
     the new token's K/V rows, the block tables and context lengths from host
-    memory (page-locked, so they are copied to HBM directly), appends the new
-    rows at position ctx - 1, decodes every sequence and copies the output back
-    (synchronous). Host wall clock around each call."""
+    memory (page-locked and mapped, so a prologue kernel reads them over the
+    bus), appends the new rows at position ctx - 1, decodes every sequence and
+    writes the output into the host array (synchronous). Host wall clock around
+    each call."""
     import torch
 
     num_seqs, q_heads, head_dim = batch.queries.shape
@@ -405,9 +406,11 @@ def run_decode_e2e(args, batch, pool, workspace, flush, device, dist, bytes_per_
             "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
             "ms_per_step": round(total / args.steps * 1e3, 5),
             "gpu_launches_per_step": 2,
-            "path": "inferlab_cuda_decode_step_host with page-locked host arrays: H2D copies "
-                    "straight from them, kv_append, paged decode, D2H straight into the "
-                    "host output; host wall clock per call"}
+            "path": "inferlab_cuda_decode_step_host with page-locked host arrays: a prologue "
+                    "kernel reads them over the bus (appends the new K/V rows, stages q, "
+                    "tables and lengths in HBM), the paged decode writes the output straight "
+                    "into the host array, a 4-byte copy returns the error word; host wall "
+                    "clock per call"}
 
 
 def host_threads() -> int:

@@ -231,11 +231,15 @@ int inferlab_cuda_paged_decode_noalloc(InferlabCudaKvPool* pool, const float* qu
  * [num_seqs][kv_heads][head_dim] (both NULL to skip the append), block_tables
  * [num_seqs][max_blocks_per_seq], context_lens [num_seqs] (the new token sits
  * at position context_lens[i] - 1 and attends to [0, context_lens[i])), out
- * [num_seqs][q_heads][head_dim]; all host memory, fp32 / int32. Inputs cross
- * to HBM in one copy from the pool's pinned staging, then kv_append, one
- * decode launch, one copy back; waits at most timeout_ms (0 = 10 s). Block
- * ids and context lengths are checked on the host first (the reference's
- * materialize checks, :776-789).
+ * [num_seqs][q_heads][head_dim]; all host memory, fp32 / int32. When every
+ * array is page-locked (cudaHostAlloc / cudaHostRegister) a prologue kernel
+ * reads them over the bus, appending the new rows and staging the decode's
+ * inputs, and the decode writes straight into `out`: two launches and a
+ * 4-byte copy. Otherwise the inputs cross to HBM by copies (through the
+ * pool's pinned staging for pageable arrays), then kv_append, one decode
+ * launch, one copy back. Waits at most timeout_ms (0 = 10 s). Block ids and
+ * context lengths are checked on the host first (the reference's materialize
+ * checks, :776-789).
  */
 int inferlab_cuda_decode_step_host(InferlabCudaKvPool* pool, const float* queries,
                                    const float* new_keys, const float* new_values,

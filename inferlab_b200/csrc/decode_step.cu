@@ -5,10 +5,14 @@
 // 713-767), gather the pages (materialize, :769-803) and call
 // attention_forward (:1458-1470), once for every active sequence
 // (worker/src/scheduler.rs:268-270). inferlab_cuda_decode_step_host is that
-// whole step for a batch in one synchronous call: the step's inputs are packed
-// into pinned staging and cross to HBM in one copy, kv_append writes every new
-// row, one decode launch covers all sequences, and one copy brings the output
-// and the pool's error word back. The K/V history stays in the HBM pool.
+// whole step for a batch in one synchronous call. When the caller's arrays are
+// page-locked and mapped, a prologue kernel reads them over the bus (appending
+// every new row and staging the decode's inputs), one decode launch covers all
+// sequences and writes the output straight into the caller's array, and a
+// 4-byte copy brings the pool's error word back. Otherwise the inputs cross to
+// HBM by copies (packed into pinned staging for pageable arrays), kv_append
+// writes the rows, and the output comes back by copy. The K/V history stays
+// in the HBM pool.
 #include "common.cuh"
 #include "internal.cuh"
 #include "pool.cuh"
@@ -84,6 +88,121 @@ void reserve_step(InferlabCudaKvPool& p, std::size_t bytes, cudaStream_t stream)
     p.step_capacity = grown;
 }
 
+// Device-accessible address of page-locked host memory (mapped into the
+// current device's address space), or nullptr.
+const void* mapped_host(const void* ptr) {
+    cudaPointerAttributes attr{};
+    if (cudaPointerGetAttributes(&attr, ptr) != cudaSuccess) {
+        cudaGetLastError();
+        return nullptr;
+    }
+    return attr.type == cudaMemoryTypeHost ? attr.devicePointer : nullptr;
+}
+
+// The fused step prologue reads the caller's page-locked arrays over the bus
+// itself (no copy calls): CTAs [0, num_seqs) append one sequence's new K/V
+// row each, the rest copy the queries, tables and lengths into device staging
+// for the decode launch and zero its split counters.
+struct StepPrologue {
+    const unsigned char* src[3];
+    unsigned char* dst[3];
+    std::size_t bytes[3];
+    std::uint32_t* counters;
+    std::size_t counter_words;
+    const float* keys;    // host-mapped [num_seqs][kv_heads * head_dim]
+    const float* values;
+    const std::int32_t* lens;    // host-mapped [num_seqs]
+    const std::int32_t* tables;  // host-mapped [num_seqs][max_blocks]
+    std::uint32_t max_blocks;
+    void* key_arena;
+    void* value_arena;
+    std::uint64_t num_blocks;
+    std::uint32_t kv_heads, block_tokens, head_dim;
+    std::uint32_t append_ctas;  // num_seqs when rows are appended, else 0
+    std::uint32_t copy_ctas;
+    std::uint32_t* error_word;
+};
+
+constexpr int kPrologueThreads = 256;
+constexpr int kPrologueCopyCtas = 64;
+
+__device__ __forceinline__ void copy_range(const unsigned char* src, unsigned char* dst, std::size_t bytes,
+                                           std::size_t t, std::size_t stride) {
+    if (((reinterpret_cast<std::uintptr_t>(src) | reinterpret_cast<std::uintptr_t>(dst) | bytes) & 15) == 0) {
+        const auto* s4 = reinterpret_cast<const uint4*>(src);
+        auto* d4 = reinterpret_cast<uint4*>(dst);
+        for (std::size_t i = t; i < bytes / 16; i += stride) d4[i] = s4[i];
+    } else {
+        // Every staged array is a whole number of 4-byte elements.
+        const auto* s1 = reinterpret_cast<const std::uint32_t*>(src);
+        auto* d1 = reinterpret_cast<std::uint32_t*>(dst);
+        for (std::size_t i = t; i < bytes / 4; i += stride) d1[i] = s1[i];
+    }
+}
+
+template <typename PoolT>
+__global__ void __launch_bounds__(kPrologueThreads) step_prologue_kernel(const StepPrologue p) {
+    if (blockIdx.x >= p.append_ctas) {
+        const std::size_t t = static_cast<std::size_t>(blockIdx.x - p.append_ctas) * blockDim.x + threadIdx.x;
+        const std::size_t stride = static_cast<std::size_t>(p.copy_ctas) * blockDim.x;
+#pragma unroll
+        for (int r = 0; r < 3; ++r) copy_range(p.src[r], p.dst[r], p.bytes[r], t, stride);
+        for (std::size_t i = t; i < p.counter_words; i += stride) p.counters[i] = 0u;
+        return;
+    }
+    // Append: the row lands in shared memory first, so a non-finite element
+    // rejects the whole row before any of it is written (the reference's
+    // prepare() rejects non-finite K/V, kernels/attention_cpu.cpp:131-134).
+    extern __shared__ float row_buf[];  // [2][width]
+    __shared__ std::int32_t block_slot[2];
+    const std::size_t s = blockIdx.x;
+    const std::size_t width = static_cast<std::size_t>(p.kv_heads) * p.head_dim;
+    bool bad = false;
+    for (std::size_t i = threadIdx.x; i < width; i += blockDim.x) {
+        const float k = p.keys[s * width + i];
+        const float v = p.values[s * width + i];
+        bad |= !isfinite(k) || !isfinite(v);
+        row_buf[i] = k;
+        row_buf[width + i] = v;
+    }
+    if (threadIdx.x == 0) {
+        // The new token sits at the last position of the context; the host
+        // has checked 1 <= length <= max_blocks * block_tokens.
+        const std::int32_t pos = p.lens[s] - 1;
+        std::int32_t block = -1;
+        if (pos >= 0 && static_cast<std::uint32_t>(pos) / p.block_tokens < p.max_blocks) {
+            block = p.tables[s * p.max_blocks + static_cast<std::uint32_t>(pos) / p.block_tokens];
+        }
+        block_slot[0] = block;
+        block_slot[1] = pos;
+    }
+    if (__syncthreads_or(bad)) {
+        if (threadIdx.x == 0) flag_error(p.error_word, kErrNonFinite);
+        return;
+    }
+    const std::int32_t block = block_slot[0];
+    const std::int32_t pos = block_slot[1];
+    if (pos < 0 || static_cast<std::uint32_t>(pos) / p.block_tokens >= p.max_blocks) {
+        if (threadIdx.x == 0) flag_error(p.error_word, kErrPosition);
+        return;
+    }
+    if (block < 0 || static_cast<std::uint64_t>(block) >= p.num_blocks) {
+        if (threadIdx.x == 0) flag_error(p.error_word, kErrBadBlock);
+        return;
+    }
+    const std::uint32_t slot = static_cast<std::uint32_t>(pos) % p.block_tokens;
+    auto* karena = static_cast<PoolT*>(p.key_arena);
+    auto* varena = static_cast<PoolT*>(p.value_arena);
+    for (std::size_t i = threadIdx.x; i < width; i += blockDim.x) {
+        const std::size_t head = i / p.head_dim;
+        const std::size_t dim = i % p.head_dim;
+        const std::size_t dst =
+            ((static_cast<std::size_t>(block) * p.kv_heads + head) * p.block_tokens + slot) * p.head_dim + dim;
+        karena[dst] = Storage<PoolT>::from_float(row_buf[i]);
+        varena[dst] = Storage<PoolT>::from_float(row_buf[width + i]);
+    }
+}
+
 }  // namespace
 }  // namespace ilb
 
@@ -138,6 +257,75 @@ extern "C" int inferlab_cuda_decode_step_host(
         const std::size_t q_bytes = static_cast<std::size_t>(num_seqs) * q_heads * p.head_dim * 4;
         const std::size_t row_bytes = static_cast<std::size_t>(num_seqs) * p.kv_heads * p.head_dim * 4;
         const std::size_t table_bytes = static_cast<std::size_t>(num_seqs) * max_blocks_per_seq * 4;
+        // Caller buffers page-locked and mapped into the device's address
+        // space: one prologue kernel reads them over the bus (appending the
+        // new rows and staging the decode's inputs), the decode writes the
+        // output straight into the caller's buffer, and only the error word
+        // is copied back - two launches and one copy per step.
+        const void* m_q = mapped_host(queries);
+        const void* m_tables = mapped_host(block_tables);
+        const void* m_lens = mapped_host(context_lens);
+        void* m_out = const_cast<void*>(mapped_host(out));
+        const void* m_k = append ? mapped_host(new_keys) : nullptr;
+        const void* m_v = append ? mapped_host(new_values) : nullptr;
+        const std::size_t width_bytes = static_cast<std::size_t>(p.kv_heads) * p.head_dim * 8;
+        if (m_q != nullptr && m_tables != nullptr && m_lens != nullptr && m_out != nullptr &&
+            (!append || (m_k != nullptr && m_v != nullptr)) && width_bytes <= 48 * 1024 &&
+            reinterpret_cast<std::uintptr_t>(m_q) % 4 == 0 &&
+            reinterpret_cast<std::uintptr_t>(m_out) % 4 == 0) {
+            StepPrologue pr{};
+            pr.src[0] = static_cast<const unsigned char*>(m_q);
+            pr.dst[0] = d + l.q;
+            pr.bytes[0] = q_bytes;
+            pr.src[1] = static_cast<const unsigned char*>(m_tables);
+            pr.dst[1] = d + l.tables;
+            pr.bytes[1] = table_bytes;
+            pr.src[2] = static_cast<const unsigned char*>(m_lens);
+            pr.dst[2] = d + l.lens;
+            pr.bytes[2] = static_cast<std::size_t>(num_seqs) * 4;
+            pr.counters = reinterpret_cast<std::uint32_t*>(d + l.workspace);
+            pr.counter_words = decode_counter_bytes(p, num_seqs) / 4;
+            pr.keys = static_cast<const float*>(m_k);
+            pr.values = static_cast<const float*>(m_v);
+            pr.lens = static_cast<const std::int32_t*>(m_lens);
+            pr.tables = static_cast<const std::int32_t*>(m_tables);
+            pr.max_blocks = max_blocks_per_seq;
+            pr.key_arena = p.key_arena;
+            pr.value_arena = p.value_arena;
+            pr.num_blocks = p.num_blocks;
+            pr.kv_heads = p.kv_heads;
+            pr.block_tokens = p.block_tokens;
+            pr.head_dim = p.head_dim;
+            pr.append_ctas = append ? num_seqs : 0u;
+            pr.copy_ctas = kPrologueCopyCtas;
+            pr.error_word = p.error_word;
+            const unsigned grid = pr.append_ctas + pr.copy_ctas;
+            const std::size_t smem = append ? width_bytes : 0;
+            if (p.dtype == kFp32) {
+                step_prologue_kernel<float><<<grid, kPrologueThreads, smem, s>>>(pr);
+            } else if (p.dtype == kF16) {
+                step_prologue_kernel<__half><<<grid, kPrologueThreads, smem, s>>>(pr);
+            } else {
+                step_prologue_kernel<__nv_bfloat16><<<grid, kPrologueThreads, smem, s>>>(pr);
+            }
+            cuda_check(cudaGetLastError(), "step prologue launch");
+            launch_paged_decode(p, reinterpret_cast<const float*>(d + l.q),
+                                reinterpret_cast<const std::int32_t*>(d + l.tables), max_blocks_per_seq,
+                                reinterpret_cast<const std::int32_t*>(d + l.lens), num_seqs, q_heads,
+                                max_context, static_cast<float*>(m_out), d + l.workspace,
+                                p.step_capacity - l.workspace, s);
+            cuda_check(cudaMemcpyAsync(h + l.err, p.error_word, 4, cudaMemcpyDeviceToHost, s),
+                       "cudaMemcpyAsync step error word");
+            wait_stream(s, timeout_ms);
+            std::uint32_t bits = 0;
+            std::memcpy(&bits, h + l.err, 4);
+            if (bits != 0) {
+                cuda_check(cudaMemsetAsync(p.error_word, 0, 4, s), "cudaMemsetAsync error word");
+                wait_stream(s, timeout_ms);
+                throw std::runtime_error(describe_error_bits(bits));
+            }
+            return;
+        }
         // Caller buffers already page-locked: copy them straight to HBM (and
         // the output straight back) instead of through the staging buffer.
         const bool direct = is_pinned(queries) && is_pinned(block_tables) &&

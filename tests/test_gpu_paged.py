@@ -179,25 +179,29 @@ def test_decode_step_host_matches_device_calls(torch_mod, wl, oracle_mod):
     batch.pool.close()
 
 
-def test_decode_step_host_pinned_buffers_match_staged(torch_mod, wl):
-    """Page-locked caller buffers take the direct-DMA path; the result equals
-    the staged path on pageable copies of the same arrays, bit for bit."""
+@pytest.mark.parametrize("kv_dtype,q_heads,kv_heads,head_dim", [(0, 16, 4, 64), (2, 32, 8, 128)])
+def test_decode_step_host_pinned_buffers_match_staged(torch_mod, wl, kv_dtype, q_heads, kv_heads,
+                                                      head_dim):
+    """Page-locked caller buffers take the mapped path (a prologue kernel reads
+    them over the bus, the decode writes the caller's output directly); the
+    result equals the staged path on pageable copies of the same arrays, bit
+    for bit, and so does the appended row."""
     torch = torch_mod
     contexts = np.array([5, 300, 1024, 77])
     rng = np.random.Generator(np.random.PCG64(28))
-    q = rng.standard_normal((len(contexts), 16, 64), dtype=np.float32)
-    k_new = rng.standard_normal((len(contexts), 4, 64), dtype=np.float32)
-    v_new = rng.standard_normal((len(contexts), 4, 64), dtype=np.float32)
+    q = rng.standard_normal((len(contexts), q_heads, head_dim), dtype=np.float32)
+    k_new = rng.standard_normal((len(contexts), kv_heads, head_dim), dtype=np.float32)
+    v_new = rng.standard_normal((len(contexts), kv_heads, head_dim), dtype=np.float32)
 
     def pinned(a):
         t = torch.empty(a.shape, dtype=getattr(torch, str(a.dtype)), pin_memory=True)
         t.numpy()[...] = a
         return t.numpy()
 
-    results = []
+    results, rows = [], []
     for use_pinned in (False, True):
-        batch = wl.decode_batch(0, 27, len(contexts), contexts, 16, 4, 64, wl.KV_FP32,
-                                max_context_len=1024)
+        batch = wl.decode_batch(0, 27, len(contexts), contexts, q_heads, kv_heads, head_dim,
+                                kv_dtype, max_context_len=1024)
         tables = np.ascontiguousarray(batch.tables_host, dtype=np.int32)
         lens = contexts.astype(np.int32)
         args = (q, tables, lens, k_new, v_new)
@@ -207,9 +211,23 @@ def test_decode_step_host_pinned_buffers_match_staged(torch_mod, wl):
         else:
             out = np.zeros_like(q)
         got = batch.pool.decode_step_host(args[0], args[1], args[2], args[3], args[4], out=out)
+        assert got is out
         results.append(np.array(got))
+        kg, vg = batch.pool.gather(batch.block_tables[2, :64].contiguous(), 1024)
+        rows.append((kg[1023].cpu(), vg[1023].cpu()))
+        if use_pinned:
+            # a non-finite new row is rejected and leaves the pool untouched
+            bad_k = pinned(k_new)
+            bad_k[1, 0, 3] = np.inf
+            from inferlab_b200 import AttentionError
+
+            with pytest.raises(AttentionError, match="^attention input must be finite$"):
+                batch.pool.decode_step_host(args[0], args[1], args[2], bad_k, args[4], out=out)
+            kg2, _ = batch.pool.gather(batch.block_tables[1, :19].contiguous(), 300)
+            assert torch.equal(kg2[299].cpu(), kg2[299].cpu().nan_to_num())
         batch.pool.close()
     assert np.array_equal(results[0], results[1])
+    assert torch.equal(rows[0][0], rows[1][0]) and torch.equal(rows[0][1], rows[1][1])
 
 
 def test_append_then_gather_bit_exact(torch_mod, wl, oracle_mod):
