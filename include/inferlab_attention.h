@@ -249,6 +249,23 @@ int inferlab_cuda_decode_step_host(InferlabCudaKvPool* pool, const float* querie
                                    uint32_t timeout_ms, char* error, size_t error_capacity);
 
 /*
+ * inferlab_cuda_decode_step_host with the step's copy-on-write block copies
+ * fused in: block_copies [num_seqs][2] holds, per sequence, the (from, to)
+ * block pair inferlab_cuda_pages_prepare_append returned for this append
+ * (PagedKvPool::append, worker/cpp/inferlab_runtime.cpp:738-754), or
+ * (-1, -1). Each copy (both arenas, the whole block) completes before that
+ * sequence's new row is written; with page-locked arrays the copies run in
+ * the step's prologue kernel. Needs new_keys / new_values.
+ */
+int inferlab_cuda_decode_step_host_cow(InferlabCudaKvPool* pool, const float* queries,
+                                       const float* new_keys, const float* new_values,
+                                       const int32_t* block_copies, const int32_t* block_tables,
+                                       uint32_t max_blocks_per_seq, const int32_t* context_lens,
+                                       uint32_t num_seqs, uint32_t q_heads, float* out,
+                                       void* stream, uint32_t timeout_ms, char* error,
+                                       size_t error_capacity);
+
+/*
  * Decode partials for a context that is split across devices: like
  * inferlab_cuda_paged_decode, but instead of the normalised output it writes,
  * per (sequence, q-head) row r = seq * q_heads + h,

@@ -113,6 +113,8 @@ struct StepPrologue {
     const float* values;
     const std::int32_t* lens;    // host-mapped [num_seqs]
     const std::int32_t* tables;  // host-mapped [num_seqs][max_blocks]
+    const std::int32_t* block_copies;  // host-mapped [num_seqs][2] (from, to), or nullptr
+    std::size_t block_bytes;           // one block of one arena, all kv-heads
     std::uint32_t max_blocks;
     void* key_arena;
     void* value_arena;
@@ -150,12 +152,30 @@ __global__ void __launch_bounds__(kPrologueThreads) step_prologue_kernel(const S
         for (std::size_t i = t; i < p.counter_words; i += stride) p.counters[i] = 0u;
         return;
     }
+    const std::size_t s = blockIdx.x;
+    // Copy on write first: the sequence's shared tail block is copied whole
+    // into its private block (both arenas), then the new row goes there
+    // (PagedKvPool::append, worker/cpp/inferlab_runtime.cpp:738-754).
+    if (p.block_copies != nullptr) {
+        const std::int32_t from = p.block_copies[s * 2];
+        const std::int32_t to = p.block_copies[s * 2 + 1];
+        if (from >= 0) {
+            for (int arena = 0; arena < 2; ++arena) {
+                const auto* src = reinterpret_cast<const uint4*>(
+                    static_cast<const unsigned char*>(arena ? p.value_arena : p.key_arena) +
+                    static_cast<std::size_t>(from) * p.block_bytes);
+                auto* dst = reinterpret_cast<uint4*>(static_cast<unsigned char*>(arena ? p.value_arena : p.key_arena) +
+                                                     static_cast<std::size_t>(to) * p.block_bytes);
+                for (std::size_t i = threadIdx.x; i < p.block_bytes / 16; i += blockDim.x) dst[i] = src[i];
+            }
+            __syncthreads();
+        }
+    }
     // Append: the row lands in shared memory first, so a non-finite element
     // rejects the whole row before any of it is written (the reference's
     // prepare() rejects non-finite K/V, kernels/attention_cpu.cpp:131-134).
     extern __shared__ float row_buf[];  // [2][width]
     __shared__ std::int32_t block_slot[2];
-    const std::size_t s = blockIdx.x;
     const std::size_t width = static_cast<std::size_t>(p.kv_heads) * p.head_dim;
     bool bad = false;
     for (std::size_t i = threadIdx.x; i < width; i += blockDim.x) {
@@ -206,11 +226,15 @@ __global__ void __launch_bounds__(kPrologueThreads) step_prologue_kernel(const S
 }  // namespace
 }  // namespace ilb
 
-extern "C" int inferlab_cuda_decode_step_host(
-    InferlabCudaKvPool* pool, const float* queries, const float* new_keys, const float* new_values,
-    const std::int32_t* block_tables, std::uint32_t max_blocks_per_seq,
-    const std::int32_t* context_lens, std::uint32_t num_seqs, std::uint32_t q_heads, float* out,
-    void* stream, std::uint32_t timeout_ms, char* error, std::size_t error_capacity) {
+namespace ilb {
+namespace {
+
+int decode_step_host(InferlabCudaKvPool* pool, const float* queries, const float* new_keys,
+                     const float* new_values, const std::int32_t* block_copies,
+                     const std::int32_t* block_tables, std::uint32_t max_blocks_per_seq,
+                     const std::int32_t* context_lens, std::uint32_t num_seqs, std::uint32_t q_heads,
+                     float* out, void* stream, std::uint32_t timeout_ms, char* error,
+                     std::size_t error_capacity) {
     return ilb::protect(error, error_capacity, [&] {
         using namespace ilb;
         auto& p = checked_pool(pool);
@@ -245,6 +269,22 @@ extern "C" int inferlab_cuda_decode_step_host(
             max_context = std::max(max_context, static_cast<std::uint32_t>(ctx));
         }
         const bool append = new_keys != nullptr;
+        const std::size_t block_bytes =
+            static_cast<std::size_t>(p.kv_heads) * p.block_tokens * p.head_dim * p.element_bytes;
+        bool any_copy = false;
+        if (block_copies != nullptr) {
+            if (!append) throw std::runtime_error("decode step block copies need new key and value rows");
+            for (std::uint32_t s = 0; s < num_seqs; ++s) {
+                const std::int32_t from = block_copies[2 * s];
+                const std::int32_t to = block_copies[2 * s + 1];
+                if (from < 0 && to < 0) continue;
+                if (from < 0 || to < 0 || static_cast<std::uint64_t>(from) >= p.num_blocks ||
+                    static_cast<std::uint64_t>(to) >= p.num_blocks || from == to) {
+                    throw std::runtime_error("paged KV block table contains an invalid page");
+                }
+                any_copy = true;
+            }
+        }
         const std::size_t ws_bytes = decode_workspace_bytes(p, num_seqs, q_heads, max_context);
         const StepLayout l = layout_for(p, num_seqs, q_heads, max_blocks_per_seq, append, ws_bytes);
 
@@ -268,9 +308,11 @@ extern "C" int inferlab_cuda_decode_step_host(
         void* m_out = const_cast<void*>(mapped_host(out));
         const void* m_k = append ? mapped_host(new_keys) : nullptr;
         const void* m_v = append ? mapped_host(new_values) : nullptr;
+        const void* m_copies = any_copy ? mapped_host(block_copies) : nullptr;
         const std::size_t width_bytes = static_cast<std::size_t>(p.kv_heads) * p.head_dim * 8;
         if (m_q != nullptr && m_tables != nullptr && m_lens != nullptr && m_out != nullptr &&
-            (!append || (m_k != nullptr && m_v != nullptr)) && width_bytes <= 48 * 1024 &&
+            (!append || (m_k != nullptr && m_v != nullptr)) && (!any_copy || m_copies != nullptr) &&
+            block_bytes % 16 == 0 && width_bytes <= 48 * 1024 &&
             reinterpret_cast<std::uintptr_t>(m_q) % 4 == 0 &&
             reinterpret_cast<std::uintptr_t>(m_out) % 4 == 0) {
             StepPrologue pr{};
@@ -289,6 +331,8 @@ extern "C" int inferlab_cuda_decode_step_host(
             pr.values = static_cast<const float*>(m_v);
             pr.lens = static_cast<const std::int32_t*>(m_lens);
             pr.tables = static_cast<const std::int32_t*>(m_tables);
+            pr.block_copies = static_cast<const std::int32_t*>(m_copies);
+            pr.block_bytes = block_bytes;
             pr.max_blocks = max_blocks_per_seq;
             pr.key_arena = p.key_arena;
             pr.value_arena = p.value_arena;
@@ -368,6 +412,16 @@ extern "C" int inferlab_cuda_decode_step_host(
         cuda_check(cudaMemsetAsync(d + l.workspace, 0, decode_counter_bytes(p, num_seqs), s),
                    "cudaMemsetAsync step workspace");
         const auto* d_tables = reinterpret_cast<const std::int32_t*>(d + l.tables);
+        for (std::uint32_t i = 0; any_copy && i < num_seqs; ++i) {
+            if (block_copies[2 * i] < 0) continue;
+            for (unsigned char* arena : {static_cast<unsigned char*>(p.key_arena),
+                                         static_cast<unsigned char*>(p.value_arena)}) {
+                cuda_check(cudaMemcpyAsync(arena + static_cast<std::size_t>(block_copies[2 * i + 1]) * block_bytes,
+                                           arena + static_cast<std::size_t>(block_copies[2 * i]) * block_bytes,
+                                           block_bytes, cudaMemcpyDeviceToDevice, s),
+                           "cudaMemcpyAsync block copy");
+            }
+        }
         if (append) {
             launch_kv_append(p, d + l.k, d + l.v, kFp32,
                              reinterpret_cast<const std::int32_t*>(d + l.seq),
@@ -400,4 +454,28 @@ extern "C" int inferlab_cuda_decode_step_host(
         }
         if (!direct) std::memcpy(out, h + l.out, q_bytes);
     });
+}
+
+}  // namespace
+}  // namespace ilb
+
+extern "C" int inferlab_cuda_decode_step_host(
+    InferlabCudaKvPool* pool, const float* queries, const float* new_keys, const float* new_values,
+    const std::int32_t* block_tables, std::uint32_t max_blocks_per_seq,
+    const std::int32_t* context_lens, std::uint32_t num_seqs, std::uint32_t q_heads, float* out,
+    void* stream, std::uint32_t timeout_ms, char* error, std::size_t error_capacity) {
+    return ilb::decode_step_host(pool, queries, new_keys, new_values, nullptr, block_tables,
+                                 max_blocks_per_seq, context_lens, num_seqs, q_heads, out, stream,
+                                 timeout_ms, error, error_capacity);
+}
+
+extern "C" int inferlab_cuda_decode_step_host_cow(
+    InferlabCudaKvPool* pool, const float* queries, const float* new_keys, const float* new_values,
+    const std::int32_t* block_copies, const std::int32_t* block_tables,
+    std::uint32_t max_blocks_per_seq, const std::int32_t* context_lens, std::uint32_t num_seqs,
+    std::uint32_t q_heads, float* out, void* stream, std::uint32_t timeout_ms, char* error,
+    std::size_t error_capacity) {
+    return ilb::decode_step_host(pool, queries, new_keys, new_values, block_copies, block_tables,
+                                 max_blocks_per_seq, context_lens, num_seqs, q_heads, out, stream,
+                                 timeout_ms, error, error_capacity);
 }

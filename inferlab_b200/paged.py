@@ -216,10 +216,14 @@ class CudaKvPool:
         return out
 
     def decode_step_host(self, queries, block_tables, context_lens, new_keys=None,
-                         new_values=None, out=None, stream=None, timeout_ms: int = 0):
+                         new_values=None, out=None, stream=None, timeout_ms: int = 0,
+                         block_copies=None):
         """One synchronous decode step from host (numpy) arrays: append the new
         token rows at context_lens - 1 (if given), decode every sequence, return
-        the output as a host array. One C call (inferlab_cuda_decode_step_host)."""
+        the output as a host array. One C call (inferlab_cuda_decode_step_host).
+        block_copies: per sequence the (from, to) copy-on-write pair that
+        PageManager.prepare_append returned, or (-1, -1); the copies run in the
+        same call before the rows are written (inferlab_cuda_decode_step_host_cow)."""
         import numpy as np
 
         q = np.ascontiguousarray(queries, dtype=np.float32)
@@ -233,10 +237,22 @@ class CudaKvPool:
         keys = None if new_keys is None else np.ascontiguousarray(new_keys, dtype=np.float32)
         values = None if new_values is None else np.ascontiguousarray(new_values, dtype=np.float32)
         error = _lib.error_buffer()
-        _check(self._lib.inferlab_cuda_decode_step_host(
+        if block_copies is None:
+            _check(self._lib.inferlab_cuda_decode_step_host(
+                self._handle, q.ctypes.data_as(f32),
+                None if keys is None else keys.ctypes.data_as(f32),
+                None if values is None else values.ctypes.data_as(f32),
+                tables.ctypes.data_as(i32), tables.shape[1], lens.ctypes.data_as(i32), num_seqs,
+                q_heads, out.ctypes.data_as(f32), _stream_handle(self.device, stream), timeout_ms,
+                error, len(error)), error)
+            return out
+        copies = np.ascontiguousarray(block_copies, dtype=np.int32)
+        if copies.shape != (num_seqs, 2):
+            raise AttentionError("decode step block copies must be [num_seqs][2]")
+        _check(self._lib.inferlab_cuda_decode_step_host_cow(
             self._handle, q.ctypes.data_as(f32),
             None if keys is None else keys.ctypes.data_as(f32),
-            None if values is None else values.ctypes.data_as(f32),
+            None if values is None else values.ctypes.data_as(f32), copies.ctypes.data_as(i32),
             tables.ctypes.data_as(i32), tables.shape[1], lens.ctypes.data_as(i32), num_seqs,
             q_heads, out.ctypes.data_as(f32), _stream_handle(self.device, stream), timeout_ms,
             error, len(error)), error)
