@@ -20,7 +20,10 @@ continuous-batching step), longseq_split (one 131,072-token sequence split
 across ranks, NCCL merge), single_seq_fp32 (the drop-in C entry
 inferlab_attention_forward with host buffers on one 129 x 4 x 32 sequence:
 prefill of 128 queries plus one decode query; launch-bound, microseconds per
-call, no roofline claim).
+call, no roofline claim), qkv_append_bf16 (the Q/K/V projection of the mixed
+step's 4 x 512 chunk tokens, model_dim 4096, with the K/V rows appended to
+the pool in the same launch; TFLOP/s, CPU baseline the reference's own fp32
+linear on one thread).
 
 --impl reference times the reference's own CPU kernel
 (oracle/_ref/libref.so, compiled from kernels/attention_cpu.cpp) on the same
@@ -251,6 +254,8 @@ def run_ours(args):
         return run_prefill(args, dist, world, rank, device, peaks, peak_kind)
     if args.workload == "mixed_bf16":
         return run_mixed(args, dist, world, rank, device, peaks, peak_kind)
+    if args.workload == "qkv_append_bf16":
+        return run_projection(args, dist, world, rank, device, peaks, peak_kind)
     if args.workload == "single_seq_fp32":
         return run_single_sequence(args, dist, world, rank, device)
     if args.workload == "longseq_split":
@@ -595,6 +600,106 @@ def run_prefill(args, dist, world, rank, device, peaks, peak_kind):
         dist.destroy_process_group()
 
 
+def cpu_projection_baseline(batch, seconds: float):
+    """The reference's own fp32 linear (oracle/_ref/libref_linear.so, built
+    from worker/cpp/inferlab_runtime.cpp:1266-1285; one thread, as the
+    reference runs it) over a bounded sample of the step's tokens; falls back
+    to the oracle's restatement of the same loop."""
+    from oracle import projection
+
+    w = batch.weights.float().cpu().numpy()
+    rows = 8
+    x = batch.hidden[:rows].float().cpu().numpy()
+    kind, fn = "reference", projection.ref_linear
+    if projection.ref_linear(x[:1], w[:64]) is None:
+        kind, fn = "port", projection.linear
+    done, t0 = 0, time.perf_counter()
+    while True:
+        fn(x, w)
+        done += 1
+        if time.perf_counter() - t0 >= seconds:
+            break
+    elapsed = time.perf_counter() - t0
+    flops = 2.0 * rows * w.shape[0] * w.shape[1] * done
+    return {"value": round(flops / elapsed / 1e12, 6), "unit": "TFLOP/s", "cores": 1, "kind": kind,
+            "cpu_model": cpu_model(),
+            "sample": f"{done} x {rows} tokens of the step through linear() "
+                      f"({w.shape[0]} x {w.shape[1]} fp32 weights) in {elapsed:.1f} s, one thread"}
+
+
+def run_projection(args, dist, world, rank, device, peaks, peak_kind):
+    """Q/K/V projection + paged K/V append of the mixed step's 4 x 512 chunk
+    tokens (inferlab_cuda_qkv_project_append), TFLOP/s of the GEMM."""
+    import torch
+
+    from inferlab_b200 import workloads as wl
+
+    batch = wl.qkv_append_bf16(device=device, seed=2030 + rank)
+    pool = batch.pool
+    stream = torch.cuda.current_stream(device)
+    flops = batch.flops()
+    q_out = torch.empty((batch.hidden.shape[0], batch.q_heads, 128), dtype=torch.bfloat16,
+                        device=f"cuda:{device}")
+    flush = L2Flush(device)
+
+    def step():
+        pool.project_append(batch.hidden, batch.weights, batch.q_heads, batch.row_sequences,
+                            batch.positions, batch.block_tables, q_out=q_out)
+
+    for i in range(args.warmup):
+        flush.fill_(float(i))
+        step()
+    pool.synchronize()
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    barrier(dist)
+    torch.cuda.synchronize(device)
+    with ClockSampler(device) as clocks:
+        preroll_end = time.perf_counter() + 0.5
+        while time.perf_counter() < preroll_end:
+            flush.fill_(0.0)
+            step()
+            stream.synchronize()
+        torch.cuda._sleep(int(2e6 + 3e5 * args.steps))
+        for i in range(args.steps):
+            flush.fill_(float(i))
+            starts[i].record(stream)
+            step()
+            ends[i].record(stream)
+        torch.cuda.synchronize(device)
+        barrier(dist)
+    pool.synchronize()
+    kernel_ms = sum(s.elapsed_time(e) for s, e in zip(starts, ends))
+    total_ms = max_over_ranks(dist, kernel_ms)
+    value = sum_over_ranks(dist, float(flops) * args.steps) / (total_ms * 1e-3) / 1e12
+    achieved = flops / (kernel_ms / args.steps * 1e-3) / 1e12
+    peak = float(peaks["bf16_tflops"])
+    line = {
+        "metric": "qkv projection + paged append TFLOP/s", "value": round(value, 3),
+        "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(total_ms / args.steps, 5), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded N(0,1) hidden, N(0,1)/sqrt(4096) weights)",
+        "config": {"workload": "Q/K/V projection of 4 x 512 chunk tokens, model_dim 4096, "
+                               "GQA 32/8 x 128 (N = 6144), K/V rows appended to a bf16 pool",
+                   "flops_per_step": int(flops),
+                   "l2": "flushed between steps: 256 MB write then 256 MB read of a second "
+                         "buffer, outside the step events"},
+        "roofline": {"bound": "tensor", "achieved": round(achieved, 2), "peak": peak,
+                     "unit": "TFLOP/s", "frac": round(achieved / peak, 4),
+                     "peak_kind": f"{peak_kind} bf16_tflops",
+                     "traffic": read_traffic("qkv_append_qkv_append_bf16")},
+        "gpu_launches": args.steps, "clocks": clocks.summary(),
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_projection_baseline(batch, min(args.cpu_seconds, 10.0))
+    pool.close()
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if dist is not None:
+        dist.destroy_process_group()
+
+
 # ---------------------------------------------------------------------------
 # reference arm
 # ---------------------------------------------------------------------------
@@ -803,7 +908,7 @@ def main():
     parser.add_argument("--impl", choices=["ours", "reference"], default="ours")
     parser.add_argument("--workload", default="decode_fp32",
                         choices=["decode_fp32", "longctx_bf16", "prefill_f16", "mixed_bf16",
-                                 "longseq_split", "single_seq_fp32"])
+                                 "longseq_split", "single_seq_fp32", "qkv_append_bf16"])
     parser.add_argument("--cpu-seconds", type=float, default=10.0)
     parser.add_argument("--no-cpu-baseline", action="store_true")
     args = parser.parse_args()

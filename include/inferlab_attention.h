@@ -157,6 +157,31 @@ int inferlab_cuda_kv_append(InferlabCudaKvPool* pool, const void* key_rows, cons
                             size_t error_capacity);
 
 /*
+ * The Q/K/V projection beside attention, with the K/V rows appended in the
+ * same launch: the three fp32 `linear` calls of the reference's forward pass
+ * (worker/cpp/inferlab_runtime.cpp:1318-1325, linear at :1266-1285) plus the
+ * PagedKvPool::append of their K/V rows (:713-767), on the tensor cores.
+ * hidden [tokens][model_dim] and weights [(q_heads + 2 kv_heads) head_dim]
+ * [model_dim] (the stacked W_q, W_k, W_v, one output feature per row) are in
+ * the pool's type (F16 or BF16 pools); products accumulate in fp32 and are
+ * rounded to the pool type. Q goes to q_out [tokens][q_heads][head_dim] (pool
+ * type); token t's K and V rows go to position positions[t] of sequence
+ * row_sequences[t] (< num_seqs) through block_tables [num_seqs]
+ * [max_blocks_per_seq]. head_dim must be a multiple of 32, model_dim of 8;
+ * hidden, weights and q_out 16-byte aligned. Device memory, asynchronous on
+ * `stream`; a bad position or block id ("paged KV append position is outside
+ * the block table", "paged KV block table contains an invalid page") skips
+ * that token's K/V rows, a non-finite K/V value is reported ("attention input
+ * must be finite") - both through the pool's error word.
+ */
+int inferlab_cuda_qkv_project_append(InferlabCudaKvPool* pool, const void* hidden,
+                                     const void* weights, uint32_t tokens, uint32_t model_dim,
+                                     uint32_t q_heads, const int32_t* row_sequences,
+                                     const int32_t* positions, const int32_t* block_tables,
+                                     uint32_t num_seqs, uint32_t max_blocks_per_seq, void* q_out,
+                                     void* stream, char* error, size_t error_capacity);
+
+/*
  * Copies the first `tokens` positions of one sequence into contiguous
  * [tokens][kv_heads][head_dim] arrays of the pool's type, bit for bit: the
  * device form of PagedKvPool::materialize (worker/cpp/inferlab_runtime.cpp:

@@ -153,6 +153,38 @@ class CudaKvPool:
             _vp(positions), rows, _vp(block_tables), block_tables.shape[-1],
             _stream_handle(dev, stream), error, len(error)), error)
 
+    def project_append(self, hidden: torch.Tensor, weights: torch.Tensor, q_heads: int,
+                       row_sequences: torch.Tensor, positions: torch.Tensor,
+                       block_tables: torch.Tensor, q_out: torch.Tensor | None = None,
+                       stream=None) -> torch.Tensor:
+        """Q/K/V projection of hidden [tokens][model_dim] by the stacked
+        weights [(q_heads + 2 kv_heads) head_dim][model_dim] (pool type, F16 or
+        BF16 pools): returns Q [tokens][q_heads][head_dim] and writes every
+        token's K/V rows into the pool at (row_sequences[t], positions[t])
+        (inferlab_cuda_qkv_project_append)."""
+        dev = self.device
+        dtype = TORCH_DTYPES.get(self.dtype)
+        _require(hidden, "hidden", dtype, dev)
+        _require(weights, "weights", dtype, dev)
+        _require(row_sequences, "row_sequences", torch.int32, dev)
+        _require(positions, "positions", torch.int32, dev)
+        _require(block_tables, "block_tables", torch.int32, dev)
+        tokens, model_dim = hidden.shape
+        if weights.shape != ((q_heads + 2 * self.kv_heads) * self.head_dim, model_dim) or \
+                row_sequences.numel() != tokens or positions.numel() != tokens or \
+                block_tables.dim() != 2:
+            raise AttentionError("projection shapes do not match the pool")
+        if q_out is None:
+            q_out = torch.empty((tokens, q_heads, self.head_dim), dtype=dtype, device=f"cuda:{dev}")
+        _require(q_out, "q_out", dtype, dev)
+        error = _lib.error_buffer()
+        _check(self._lib.inferlab_cuda_qkv_project_append(
+            self._handle, _vp(hidden), _vp(weights), tokens, model_dim, q_heads,
+            _vp(row_sequences), _vp(positions), _vp(block_tables), block_tables.shape[0],
+            block_tables.shape[1], _vp(q_out), _stream_handle(dev, stream), error, len(error)),
+            error)
+        return q_out
+
     def gather(self, block_table: torch.Tensor, tokens: int, stream=None):
         """Contiguous copies [tokens][kv_heads][head_dim] of one sequence's K and V."""
         dev = self.device

@@ -244,6 +244,50 @@ def mixed_bf16(device: int = 0, seed: int = 2029, num_decode: int = 32, num_chun
         offsets_dev=torch.from_numpy(offsets).to(dev))
 
 
+@dataclass
+class ProjectionBatch:
+    pool: CudaKvPool
+    hidden: torch.Tensor        # [tokens][model_dim], pool type
+    weights: torch.Tensor       # [(q_heads + 2 kv_heads) head_dim][model_dim], pool type
+    q_heads: int
+    row_sequences: torch.Tensor
+    positions: torch.Tensor
+    block_tables: torch.Tensor
+    tables_host: np.ndarray
+
+    def flops(self) -> int:
+        return 2 * self.hidden.shape[0] * self.weights.shape[0] * self.hidden.shape[1]
+
+
+def qkv_append_bf16(device: int = 0, seed: int = 2030, num_chunks: int = 4,
+                    chunk_tokens: int = 512, model_dim: int = 4096,
+                    num_blocks: int = 16384) -> ProjectionBatch:
+    """The projection beside a continuous-batching step's prefill chunks:
+    num_chunks x chunk_tokens tokens (positions [prior, prior + chunk_tokens)
+    with prior from the clipped Zipf of the mixed step), hidden states
+    N(0, 1) of model_dim 4096, stacked W_q / W_k / W_v for GQA 32 q / 8 kv
+    heads x 128 (N = 6144) scaled by 1/sqrt(model_dim), bf16; the K/V rows go
+    to a pool of num_blocks blocks through seeded tables."""
+    rng = np.random.Generator(np.random.PCG64(seed))
+    priors = zipf_contexts(rng, num_chunks)
+    need = (priors + chunk_tokens + BLOCK_TOKENS - 1) // BLOCK_TOKENS
+    max_blocks = int(need.max())
+    tables = _deal_tables(rng, num_blocks, need, max_blocks)
+    pool = CudaKvPool(device, KV_BF16, num_blocks, BLOCK_TOKENS, 8, 128)
+    gen = _generator(seed + 1, device)
+    dev = f"cuda:{device}"
+    tokens = num_chunks * chunk_tokens
+    hidden = torch.randn((tokens, model_dim), generator=gen, device=dev).to(torch.bfloat16)
+    weights = (torch.randn(((32 + 16) * 128, model_dim), generator=gen, device=dev) /
+               model_dim ** 0.5).to(torch.bfloat16)
+    seq = np.repeat(np.arange(num_chunks, dtype=np.int32), chunk_tokens)
+    pos = np.concatenate([np.arange(p, p + chunk_tokens, dtype=np.int32) for p in priors])
+    return ProjectionBatch(pool=pool, hidden=hidden, weights=weights, q_heads=32,
+                           row_sequences=torch.from_numpy(seq).to(dev),
+                           positions=torch.from_numpy(pos).to(dev),
+                           block_tables=torch.from_numpy(tables).to(dev), tables_host=tables)
+
+
 def long_sequence_shard(device: int, rank: int, world: int, total_tokens: int = 131072,
                         seed: int = 2030) -> PagedBatch:
     """One total_tokens-token sequence (GQA 32/8 x 128, bf16) whose blocks are

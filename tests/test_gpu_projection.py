@@ -1,0 +1,99 @@
+"""inferlab_cuda_qkv_project_append against the projection oracle
+(oracle/projection.py: the reference's fp32 linear, pinned bit for bit, and
+PagedKvPool::append's placement). The GPU multiplies the pool-type (f16 /
+bf16) operands with fp32 accumulation and rounds to the pool type, so every
+element must satisfy |gpu - ref| <= 2^-7 |ref| + 2^-8 rms(ref) (a little over
+one rounding step of bf16) against the fp32 oracle fed the same rounded
+operands; tokens' K/V rows must sit exactly where the block tables say."""
+import numpy as np
+import pytest
+
+from oracle import projection
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def torch_mod():
+    import torch
+
+    assert torch.cuda.is_available(), "these tests need a CUDA device"
+    return torch
+
+
+def _case(torch, dtype, tokens, model_dim, q_heads, kv_heads, head_dim, seed):
+    from inferlab_b200 import CudaKvPool
+    from inferlab_b200 import workloads as wl
+
+    tdt = wl.TORCH_DTYPES[dtype]
+    dev = "cuda:0"
+    pool = CudaKvPool(0, dtype, 256, 16, kv_heads, head_dim)
+    rng = np.random.Generator(np.random.PCG64(seed))
+    gen = torch.Generator(device=dev).manual_seed(seed)
+    hidden = torch.randn((tokens, model_dim), generator=gen, device=dev).to(tdt)
+    n = (q_heads + 2 * kv_heads) * head_dim
+    weights = (torch.randn((n, model_dim), generator=gen, device=dev) / model_dim ** 0.5).to(tdt)
+    # three sequences, each a run of consecutive positions (a prefill chunk)
+    starts = [0, 40, 7]
+    counts = [tokens // 3, tokens // 3, tokens - 2 * (tokens // 3)]
+    seq = np.concatenate([np.full(c, s, np.int32) for s, c in enumerate(counts)])
+    pos = np.concatenate([np.arange(st, st + c, dtype=np.int32) for st, c in zip(starts, counts)])
+    max_blocks = int((pos.max() + 16) // 16)
+    tables = rng.permutation(256)[:3 * max_blocks].astype(np.int32).reshape(3, max_blocks)
+    q = pool.project_append(hidden, weights, q_heads,
+                            torch.from_numpy(seq).to(dev), torch.from_numpy(pos).to(dev),
+                            torch.from_numpy(tables).to(dev))
+    pool.synchronize()
+    x32 = hidden.float().cpu().numpy()
+    w32 = weights.float().cpu().numpy()
+    rq, rk, rv, blocks, slots = projection.project_append(
+        x32, w32, q_heads, kv_heads, head_dim, seq, pos, tables, 16)
+
+    def close(got, ref):
+        tol = 2.0 ** -7 * np.abs(ref) + 2.0 ** -8 * float(np.sqrt(np.mean(ref ** 2)))
+        assert np.all(np.abs(got - ref) <= tol), float(np.max(np.abs(got - ref) - tol))
+
+    close(q.float().cpu().numpy(), rq)
+    karena = pool.key_arena.float().cpu().numpy()    # [blocks][kv_heads][16][d]
+    varena = pool.value_arena.float().cpu().numpy()
+    close(karena[blocks, :, slots, :], rk)
+    close(varena[blocks, :, slots, :], rv)
+    # nothing else of the pool was written
+    mask = np.zeros(karena.shape[0] * 16, bool)
+    mask[blocks * 16 + slots] = True
+    rest = karena.transpose(0, 2, 1, 3).reshape(-1, kv_heads * head_dim)[~mask]
+    assert not np.any(rest)
+    pool.close()
+
+
+@pytest.mark.parametrize("dtype", [1, 2])
+def test_projection_gqa_ragged_tokens(torch_mod, dtype):
+    # 300 tokens (last 128-token tile ragged), 8 q / 2 kv heads x 128: N = 1536
+    _case(torch_mod, dtype, 300, 256, 8, 2, 128, 5)
+
+
+def test_projection_small_heads_partial_feature_tile(torch_mod):
+    # the single-sequence configuration's shape: 4 heads x 32 (N = 384, a
+    # partial 256-feature tile), model_dim 200 (a partial 64-wide K stage)
+    _case(torch_mod, 2, 129, 200, 4, 4, 32, 6)
+
+
+def test_projection_rejects_bad_block(torch_mod):
+    import torch
+
+    from inferlab_b200 import AttentionError, CudaKvPool
+
+    dev = "cuda:0"
+    pool = CudaKvPool(0, 2, 8, 16, 1, 32)
+    hidden = torch.ones((4, 64), dtype=torch.bfloat16, device=dev)
+    weights = torch.ones((3 * 32, 64), dtype=torch.bfloat16, device=dev)
+    tables = torch.tensor([[99]], dtype=torch.int32, device=dev)
+    pool.project_append(hidden, weights, 1, torch.zeros(4, dtype=torch.int32, device=dev),
+                        torch.arange(4, dtype=torch.int32, device=dev), tables)
+    with pytest.raises(AttentionError, match="^paged KV block table contains an invalid page$"):
+        pool.synchronize()
+    with pytest.raises(AttentionError, match="^projection needs an F16 or BF16 pool$"):
+        CudaKvPool(0, 0, 8, 16, 1, 32).project_append(
+            hidden.float(), weights.float(), 1, torch.zeros(4, dtype=torch.int32, device=dev),
+            torch.arange(4, dtype=torch.int32, device=dev), tables)
+    pool.close()
