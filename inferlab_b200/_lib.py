@@ -107,15 +107,16 @@ SIGNATURES = {
     "inferlab_cuda_paged_decode_noalloc": (ctypes.c_int, [
         c_vp, c_vp, c_vp, ctypes.c_uint32, c_vp, ctypes.c_uint32, ctypes.c_uint32,
         ctypes.c_uint32, c_vp, c_vp, c_err, c_sz]),
+    # host-array pointers passed as plain addresses (the per-step call path)
     "inferlab_cuda_decode_step_host": (ctypes.c_int, [
-        c_vp, c_f32p, c_f32p, c_f32p, c_i32p, ctypes.c_uint32, c_i32p, ctypes.c_uint32,
-        ctypes.c_uint32, c_f32p, c_vp, ctypes.c_uint32, c_err, c_sz]),
+        c_vp, c_vp, c_vp, c_vp, c_vp, ctypes.c_uint32, c_vp, ctypes.c_uint32,
+        ctypes.c_uint32, c_vp, c_vp, ctypes.c_uint32, c_err, c_sz]),
     "inferlab_cuda_qkv_project_append": (ctypes.c_int, [
         c_vp, c_vp, c_vp, ctypes.c_uint32, ctypes.c_uint32, ctypes.c_uint32, c_vp, c_vp, c_vp,
         ctypes.c_uint32, ctypes.c_uint32, c_vp, c_vp, c_err, c_sz]),
     "inferlab_cuda_decode_step_host_cow": (ctypes.c_int, [
-        c_vp, c_f32p, c_f32p, c_f32p, c_i32p, c_i32p, ctypes.c_uint32, c_i32p, ctypes.c_uint32,
-        ctypes.c_uint32, c_f32p, c_vp, ctypes.c_uint32, c_err, c_sz]),
+        c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, ctypes.c_uint32, c_vp, ctypes.c_uint32,
+        ctypes.c_uint32, c_vp, c_vp, ctypes.c_uint32, c_err, c_sz]),
     "inferlab_cuda_paged_decode_partials": (ctypes.c_int, [
         c_vp, c_vp, c_vp, ctypes.c_uint32, c_vp, ctypes.c_uint32, ctypes.c_uint32,
         ctypes.c_uint32, c_vp, c_vp, c_vp, c_vp, c_sz, c_vp, c_err, c_sz]),

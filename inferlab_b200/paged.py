@@ -264,30 +264,29 @@ class CudaKvPool:
         num_seqs, q_heads, _ = q.shape
         if out is None:
             out = np.empty_like(q)
-        f32 = ctypes.POINTER(ctypes.c_float)
-        i32 = ctypes.POINTER(ctypes.c_int32)
+        elif not (isinstance(out, np.ndarray) and out.dtype == np.float32 and
+                  out.flags.c_contiguous and out.shape == q.shape):
+            raise AttentionError("decode step output must be a contiguous float32 array shaped "
+                                 "like the queries")
         keys = None if new_keys is None else np.ascontiguousarray(new_keys, dtype=np.float32)
         values = None if new_values is None else np.ascontiguousarray(new_values, dtype=np.float32)
         error = _lib.error_buffer()
+        # Plain addresses: the per-step path avoids ctypes pointer objects.
+        kp = None if keys is None else keys.ctypes.data
+        vp = None if values is None else values.ctypes.data
         if block_copies is None:
             _check(self._lib.inferlab_cuda_decode_step_host(
-                self._handle, q.ctypes.data_as(f32),
-                None if keys is None else keys.ctypes.data_as(f32),
-                None if values is None else values.ctypes.data_as(f32),
-                tables.ctypes.data_as(i32), tables.shape[1], lens.ctypes.data_as(i32), num_seqs,
-                q_heads, out.ctypes.data_as(f32), _stream_handle(self.device, stream), timeout_ms,
-                error, len(error)), error)
+                self._handle, q.ctypes.data, kp, vp, tables.ctypes.data, tables.shape[1],
+                lens.ctypes.data, num_seqs, q_heads, out.ctypes.data,
+                _stream_handle(self.device, stream), timeout_ms, error, len(error)), error)
             return out
         copies = np.ascontiguousarray(block_copies, dtype=np.int32)
         if copies.shape != (num_seqs, 2):
             raise AttentionError("decode step block copies must be [num_seqs][2]")
         _check(self._lib.inferlab_cuda_decode_step_host_cow(
-            self._handle, q.ctypes.data_as(f32),
-            None if keys is None else keys.ctypes.data_as(f32),
-            None if values is None else values.ctypes.data_as(f32), copies.ctypes.data_as(i32),
-            tables.ctypes.data_as(i32), tables.shape[1], lens.ctypes.data_as(i32), num_seqs,
-            q_heads, out.ctypes.data_as(f32), _stream_handle(self.device, stream), timeout_ms,
-            error, len(error)), error)
+            self._handle, q.ctypes.data, kp, vp, copies.ctypes.data, tables.ctypes.data,
+            tables.shape[1], lens.ctypes.data, num_seqs, q_heads, out.ctypes.data,
+            _stream_handle(self.device, stream), timeout_ms, error, len(error)), error)
         return out
 
     def decode_partials(self, queries: torch.Tensor, block_tables: torch.Tensor,

@@ -172,4 +172,10 @@ def test_pool_api_rejects_bad_arguments_without_gpu():
     assert lib.inferlab_cuda_lse_combine(None, None, None, 1, 1, 1, None, None, err, 256) == -1
     assert err.value == b"lse combine pointer is null"
     assert lib.inferlab_cuda_paged_decode_workspace_size(None, 1, 1, 1) == 0
+    assert lib.inferlab_cuda_qkv_project_append(None, None, None, 1, 64, 1, None, None, None, 1, 1,
+                                                None, None, err, 256) == -1
+    assert err.value == b"paged KV pool pointer is null"
+    assert lib.inferlab_cuda_decode_step_host_cow(None, None, None, None, None, None, 1, None, 1,
+                                                  1, None, None, 0, err, 256) == -1
+    assert err.value == b"paged KV pool pointer is null"
     lib.inferlab_cuda_pool_destroy(None)
