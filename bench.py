@@ -23,7 +23,8 @@ prefill of 128 queries plus one decode query; launch-bound, microseconds per
 call, no roofline claim), qkv_append_bf16 (the Q/K/V projection of the mixed
 step's 4 x 512 chunk tokens, model_dim 4096, with the K/V rows appended to
 the pool in the same launch; TFLOP/s, CPU baseline the reference's own fp32
-linear on one thread).
+linear on one thread), outproj_bf16 (the output projection + residual add of
+the same tokens from the fp32 attention output).
 
 --impl reference times the reference's own CPU kernel
 (oracle/_ref/libref.so, compiled from kernels/attention_cpu.cpp) on the same
@@ -254,7 +255,7 @@ def run_ours(args):
         return run_prefill(args, dist, world, rank, device, peaks, peak_kind)
     if args.workload == "mixed_bf16":
         return run_mixed(args, dist, world, rank, device, peaks, peak_kind)
-    if args.workload == "qkv_append_bf16":
+    if args.workload in ("qkv_append_bf16", "outproj_bf16"):
         return run_projection(args, dist, world, rank, device, peaks, peak_kind)
     if args.workload == "single_seq_fp32":
         return run_single_sequence(args, dist, world, rank, device)
@@ -628,8 +629,11 @@ def cpu_projection_baseline(batch, seconds: float):
 
 
 def run_projection(args, dist, world, rank, device, peaks, peak_kind):
-    """Q/K/V projection + paged K/V append of the mixed step's 4 x 512 chunk
-    tokens (inferlab_cuda_qkv_project_append), TFLOP/s of the GEMM."""
+    """qkv_append_bf16: Q/K/V projection + paged K/V append of the mixed
+    step's 4 x 512 chunk tokens (inferlab_cuda_qkv_project_append).
+    outproj_bf16: the output projection + residual add of the same tokens
+    from the fp32 attention output (inferlab_cuda_output_project, which
+    rounds its input to bf16 in the step). TFLOP/s of the GEMM."""
     import torch
 
     from inferlab_b200 import workloads as wl
@@ -637,14 +641,28 @@ def run_projection(args, dist, world, rank, device, peaks, peak_kind):
     batch = wl.qkv_append_bf16(device=device, seed=2030 + rank)
     pool = batch.pool
     stream = torch.cuda.current_stream(device)
-    flops = batch.flops()
-    q_out = torch.empty((batch.hidden.shape[0], batch.q_heads, 128), dtype=torch.bfloat16,
-                        device=f"cuda:{device}")
+    dev = f"cuda:{device}"
+    tokens, model_dim = batch.hidden.shape
+    outproj = args.workload == "outproj_bf16"
+    if outproj:
+        gen = torch.Generator(device=dev).manual_seed(2040 + rank)
+        attn = torch.randn((tokens, 32 * 128), generator=gen, device=dev)
+        w_o = (torch.randn((model_dim, 32 * 128), generator=gen, device=dev) /
+               (32 * 128) ** 0.5).to(torch.bfloat16)
+        residual = torch.randn((tokens, model_dim), generator=gen, device=dev)
+        out = torch.empty_like(residual)
+        flops = 2 * tokens * model_dim * 32 * 128
+    else:
+        flops = batch.flops()
+        q_out = torch.empty((tokens, batch.q_heads, 128), dtype=torch.bfloat16, device=dev)
     flush = L2Flush(device)
 
     def step():
-        pool.project_append(batch.hidden, batch.weights, batch.q_heads, batch.row_sequences,
-                            batch.positions, batch.block_tables, q_out=q_out)
+        if outproj:
+            pool.output_project(attn, w_o, residual, out=out)
+        else:
+            pool.project_append(batch.hidden, batch.weights, batch.q_heads, batch.row_sequences,
+                                batch.positions, batch.block_tables, q_out=q_out)
 
     for i in range(args.warmup):
         flush.fill_(float(i))
@@ -674,24 +692,36 @@ def run_projection(args, dist, world, rank, device, peaks, peak_kind):
     value = sum_over_ranks(dist, float(flops) * args.steps) / (total_ms * 1e-3) / 1e12
     achieved = flops / (kernel_ms / args.steps * 1e-3) / 1e12
     peak = float(peaks["bf16_tflops"])
+    if outproj:
+        metric = "output projection + residual TFLOP/s"
+        workload = ("output projection of 4 x 512 chunk tokens: fp32 attention output "
+                    "[2048][4096] rounded to bf16 in the step, W_o [4096][4096] bf16, fp32 "
+                    "residual add")
+        profile = "qkv_append_outproj_bf16"
+    else:
+        metric = "qkv projection + paged append TFLOP/s"
+        workload = ("Q/K/V projection of 4 x 512 chunk tokens, model_dim 4096, GQA 32/8 x 128 "
+                    "(N = 6144), K/V rows appended to a bf16 pool")
+        profile = "qkv_append_qkv_append_bf16"
     line = {
-        "metric": "qkv projection + paged append TFLOP/s", "value": round(value, 3),
+        "metric": metric, "value": round(value, 3),
         "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(total_ms / args.steps, 5), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
-        "data": "synthetic (seeded N(0,1) hidden, N(0,1)/sqrt(4096) weights)",
-        "config": {"workload": "Q/K/V projection of 4 x 512 chunk tokens, model_dim 4096, "
-                               "GQA 32/8 x 128 (N = 6144), K/V rows appended to a bf16 pool",
+        "data": "synthetic (seeded N(0,1) activations, N(0,1)/sqrt(in) weights)",
+        "config": {"workload": workload,
                    "flops_per_step": int(flops),
                    "l2": "flushed between steps: 256 MB write then 256 MB read of a second "
                          "buffer, outside the step events"},
         "roofline": {"bound": "tensor", "achieved": round(achieved, 2), "peak": peak,
                      "unit": "TFLOP/s", "frac": round(achieved / peak, 4),
                      "peak_kind": f"{peak_kind} bf16_tflops",
-                     "traffic": read_traffic("qkv_append_qkv_append_bf16")},
-        "gpu_launches": args.steps, "clocks": clocks.summary(),
+                     "traffic": read_traffic(profile)},
+        "gpu_launches": args.steps * (2 if outproj else 1), "clocks": clocks.summary(),
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        if outproj:
+            batch.hidden, batch.weights = attn.to(torch.bfloat16), w_o
         line["cpu_baseline"] = cpu_projection_baseline(batch, min(args.cpu_seconds, 10.0))
     pool.close()
     if rank == 0:
@@ -908,7 +938,8 @@ def main():
     parser.add_argument("--impl", choices=["ours", "reference"], default="ours")
     parser.add_argument("--workload", default="decode_fp32",
                         choices=["decode_fp32", "longctx_bf16", "prefill_f16", "mixed_bf16",
-                                 "longseq_split", "single_seq_fp32", "qkv_append_bf16"])
+                                 "longseq_split", "single_seq_fp32", "qkv_append_bf16",
+                                 "outproj_bf16"])
     parser.add_argument("--cpu-seconds", type=float, default=10.0)
     parser.add_argument("--no-cpu-baseline", action="store_true")
     args = parser.parse_args()

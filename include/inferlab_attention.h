@@ -182,6 +182,24 @@ int inferlab_cuda_qkv_project_append(InferlabCudaKvPool* pool, const void* hidde
                                      void* stream, char* error, size_t error_capacity);
 
 /*
+ * The output projection after attention, with the residual add: the
+ * reference's `linear(attention_context, ..., attention_output_weight, ...)`
+ * and `hidden += attention_output` (worker/cpp/inferlab_runtime.cpp:
+ * 1340-1350), on the tensor cores. attention [tokens][in_dim] (fp32, as the
+ * attention entries return it, rounded here to the pool type; or already in
+ * the pool type), weights [out_dim][in_dim] in the pool's type (F16 / BF16
+ * pools; the pool supplies the device and the error word), residual
+ * [tokens][out_dim] fp32 or NULL, out [tokens][out_dim] fp32 = residual +
+ * attention x weights^T with fp32 accumulation. in_dim a multiple of 8,
+ * out_dim of 32; buffers 16-byte aligned; device memory, asynchronous.
+ */
+int inferlab_cuda_output_project(InferlabCudaKvPool* pool, const void* attention,
+                                 uint32_t attention_dtype, const void* weights,
+                                 const float* residual, uint32_t tokens, uint32_t in_dim,
+                                 uint32_t out_dim, float* out, void* stream, char* error,
+                                 size_t error_capacity);
+
+/*
  * Copies the first `tokens` positions of one sequence into contiguous
  * [tokens][kv_heads][head_dim] arrays of the pool's type, bit for bit: the
  * device form of PagedKvPool::materialize (worker/cpp/inferlab_runtime.cpp:

@@ -114,6 +114,9 @@ SIGNATURES = {
     "inferlab_cuda_qkv_project_append": (ctypes.c_int, [
         c_vp, c_vp, c_vp, ctypes.c_uint32, ctypes.c_uint32, ctypes.c_uint32, c_vp, c_vp, c_vp,
         ctypes.c_uint32, ctypes.c_uint32, c_vp, c_vp, c_err, c_sz]),
+    "inferlab_cuda_output_project": (ctypes.c_int, [
+        c_vp, c_vp, ctypes.c_uint32, c_vp, c_vp, ctypes.c_uint32, ctypes.c_uint32,
+        ctypes.c_uint32, c_vp, c_vp, c_err, c_sz]),
     "inferlab_cuda_decode_step_host_cow": (ctypes.c_int, [
         c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, ctypes.c_uint32, c_vp, ctypes.c_uint32,
         ctypes.c_uint32, c_vp, c_vp, ctypes.c_uint32, c_err, c_sz]),

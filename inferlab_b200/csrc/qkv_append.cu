@@ -77,8 +77,14 @@ struct Params {
     unsigned char* q_out;
     unsigned char* key_arena;
     unsigned char* value_arena;
+    const float* residual;  // output projection: [T][N] fp32 added to the product, or null
+    float* out;             // output projection: [T][N] fp32
     std::uint32_t* error_word;
 };
+
+// Epilogue modes of the shared GEMM kernel.
+constexpr int kModeQkvAppend = 0;  // Q rows out, K/V rows into the pool (pool type)
+constexpr int kModeOutput = 1;     // fp32 rows out, plus an optional fp32 residual
 
 template <typename T>
 __device__ __forceinline__ std::uint32_t pack2(float lo, float hi);
@@ -93,7 +99,7 @@ __device__ __forceinline__ std::uint32_t pack2<__nv_bfloat16>(float lo, float hi
     return *reinterpret_cast<const std::uint32_t*>(&h);
 }
 
-template <typename T>
+template <typename T, int kMode>
 __global__ void __launch_bounds__(kThreads, 1)
     qkv_append_kernel(const __grid_constant__ CUtensorMap x_map,
                       const __grid_constant__ CUtensorMap w_map, const Params p) {
@@ -197,7 +203,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             bool live = token < p.tokens;
             // Where this token's K/V rows go, when the tile holds K/V columns.
             std::size_t kv_row = 0;  // (block * kv_heads) * block_tokens + slot, in rows
-            if (live && n * kBN + kBN > q_cols) {
+            if (kMode == kModeQkvAppend && live && n * kBN + kBN > q_cols) {
                 const std::int32_t seq = p.row_sequences[token];
                 const std::int32_t pos = p.positions[token];
                 if (seq < 0 || static_cast<std::uint32_t>(seq) >= p.num_seqs || pos < 0 ||
@@ -224,8 +230,22 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (f0 >= p.features) break;  // uniform: the tile's last columns lie past N
                 float v[32];
                 tmem_load32(lane_addr + b * kBN + static_cast<std::uint32_t>(c) * 32, v);
-                if (!live && f0 >= q_cols) continue;
                 if (token >= p.tokens) continue;
+                if constexpr (kMode == kModeOutput) {
+                    // out = product (+ residual), fp32, 32 consecutive columns.
+                    const std::size_t at = static_cast<std::size_t>(token) * p.features + f0;
+                    float4* o4 = reinterpret_cast<float4*>(p.out + at);
+                    const float4* r4 = reinterpret_cast<const float4*>(p.residual + at);
+#pragma unroll
+                    for (int q = 0; q < 8; ++q) {
+                        float4 r = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+                        if (p.residual != nullptr) r = r4[q];
+                        o4[q] = make_float4(v[4 * q] + r.x, v[4 * q + 1] + r.y, v[4 * q + 2] + r.z,
+                                            v[4 * q + 3] + r.w);
+                    }
+                    continue;
+                }
+                if (!live && f0 >= q_cols) continue;
                 // head_dim is a multiple of 32, so the 32 columns are one head's.
                 const std::uint32_t head = f0 / p.head_dim;
                 const std::uint32_t dim0 = f0 % p.head_dim;
@@ -342,7 +362,123 @@ extern "C" int inferlab_cuda_qkv_project_append(
         cuda_check(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, p.device),
                    "cudaDeviceGetAttribute");
         const unsigned grid = static_cast<unsigned>(std::min<std::uint64_t>(total, static_cast<std::uint64_t>(std::max(sms, 1))));
-        auto kernel = p.dtype == kBf16 ? qkv_append_kernel<__nv_bfloat16> : qkv_append_kernel<__half>;
+        auto kernel = p.dtype == kBf16 ? qkv_append_kernel<__nv_bfloat16, kModeQkvAppend>
+                                       : qkv_append_kernel<__half, kModeQkvAppend>;
+        cuda_check(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemAlloc),
+                   "cudaFuncSetAttribute");
+        kernel<<<grid, kThreads, kSmemAlloc, s>>>(x_map, w_map, prm);
+        cuda_check(cudaGetLastError(), "projection launch");
+    });
+}
+
+namespace ilb {
+namespace qkv {
+namespace {
+
+// fp32 -> pool type (round to nearest even), for attention outputs handed to
+// the output projection in fp32: eight elements per thread and step (two
+// 16-byte loads, one 16-byte store; n is a multiple of 8 since in_dim is).
+template <typename T>
+__global__ void round_rows_kernel(const float* in, T* out, std::size_t n) {
+    const auto* in4 = reinterpret_cast<const float4*>(in);
+    auto* out4 = reinterpret_cast<uint4*>(out);
+    for (std::size_t i = static_cast<std::size_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n / 8;
+         i += static_cast<std::size_t>(gridDim.x) * blockDim.x) {
+        const float4 a = in4[2 * i];
+        const float4 b = in4[2 * i + 1];
+        out4[i] = make_uint4(pack2<T>(a.x, a.y), pack2<T>(a.z, a.w), pack2<T>(b.x, b.y),
+                             pack2<T>(b.z, b.w));
+    }
+}
+
+}  // namespace
+}  // namespace qkv
+}  // namespace ilb
+
+extern "C" int inferlab_cuda_output_project(InferlabCudaKvPool* pool, const void* attention,
+                                            std::uint32_t attention_dtype, const void* weights,
+                                            const float* residual, std::uint32_t tokens,
+                                            std::uint32_t in_dim, std::uint32_t out_dim, float* out,
+                                            void* stream, char* error, std::size_t error_capacity) {
+    return ilb::protect(error, error_capacity, [&] {
+        using namespace ilb;
+        using namespace ilb::qkv;
+        auto& p = checked_pool(pool);
+        if (tokens == 0) return;
+        if (attention == nullptr || weights == nullptr || out == nullptr) {
+            throw std::runtime_error("projection pointer is null");
+        }
+        if (p.dtype != kF16 && p.dtype != kBf16) {
+            throw std::runtime_error("projection needs an F16 or BF16 pool");
+        }
+        if (attention_dtype != kFp32 && attention_dtype != p.dtype) {
+            throw std::runtime_error("projection input dtype must be FP32 or the pool dtype");
+        }
+        if (in_dim == 0 || in_dim % 8 != 0) {
+            throw std::runtime_error("projection model_dim must be a positive multiple of 8");
+        }
+        if (out_dim == 0 || out_dim % 32 != 0) {
+            throw std::runtime_error("projection output width must be a positive multiple of 32");
+        }
+        if (tokens > 0x7FFFFFFFu) throw std::runtime_error("projection is too large");
+        for (const void* ptr : {attention, weights, static_cast<const void*>(out),
+                                static_cast<const void*>(residual)}) {
+            if (reinterpret_cast<std::uintptr_t>(ptr) % 16 != 0) {
+                throw std::runtime_error("projection buffers must be 16-byte aligned");
+            }
+        }
+        DeviceGuard guard(p.device);
+        auto s = static_cast<cudaStream_t>(stream);
+        const bool bf16 = p.dtype == kBf16;
+        const void* a16 = attention;
+        void* temp = nullptr;
+        if (attention_dtype == kFp32) {
+            const std::size_t n = static_cast<std::size_t>(tokens) * in_dim;
+            cuda_check(cudaMallocAsync(&temp, n * 2, s), "cudaMallocAsync");
+            const unsigned grid = static_cast<unsigned>(std::min<std::size_t>((n / 8 + 255) / 256, 148 * 16));
+            if (bf16) {
+                round_rows_kernel<__nv_bfloat16><<<grid, 256, 0, s>>>(
+                    static_cast<const float*>(attention), static_cast<__nv_bfloat16*>(temp), n);
+            } else {
+                round_rows_kernel<__half><<<grid, 256, 0, s>>>(static_cast<const float*>(attention),
+                                                               static_cast<__half*>(temp), n);
+            }
+            cuda_check(cudaGetLastError(), "projection input rounding launch");
+            a16 = temp;
+        }
+        struct TempGuard {
+            void* ptr;
+            cudaStream_t stream;
+            ~TempGuard() {
+                if (ptr != nullptr) cudaFreeAsync(ptr, stream);
+            }
+        } guard_temp{temp, s};
+        const CUtensorMapDataType type =
+            bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+        const cuuint64_t x_dims[2] = {in_dim, tokens};
+        const cuuint64_t x_strides[1] = {static_cast<cuuint64_t>(in_dim) * 2};
+        const cuuint32_t x_box[2] = {kBK, kBM};
+        const CUtensorMap x_map = make_map(const_cast<void*>(a16), type, 2, x_dims, x_strides, x_box);
+        const cuuint64_t w_dims[2] = {in_dim, out_dim};
+        const cuuint32_t w_box[2] = {kBK, kBN};
+        const CUtensorMap w_map = make_map(const_cast<void*>(weights), type, 2, w_dims, x_strides, w_box);
+        Params prm{};
+        prm.tokens = tokens;
+        prm.features = out_dim;
+        prm.k_stages = (in_dim + kBK - 1) / kBK;
+        prm.m_tiles = (tokens + kBM - 1) / kBM;
+        prm.n_tiles = (out_dim + kBN - 1) / kBN;
+        prm.residual = residual;
+        prm.out = out;
+        prm.error_word = p.error_word;
+        const std::uint64_t total = static_cast<std::uint64_t>(prm.m_tiles) * prm.n_tiles;
+        if (total > 0x7FFFFFFFull) throw std::runtime_error("projection is too large");
+        int sms = 0;
+        cuda_check(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, p.device),
+                   "cudaDeviceGetAttribute");
+        const unsigned grid = static_cast<unsigned>(std::min<std::uint64_t>(total, static_cast<std::uint64_t>(std::max(sms, 1))));
+        auto kernel = bf16 ? qkv_append_kernel<__nv_bfloat16, kModeOutput>
+                           : qkv_append_kernel<__half, kModeOutput>;
         cuda_check(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemAlloc),
                    "cudaFuncSetAttribute");
         kernel<<<grid, kThreads, kSmemAlloc, s>>>(x_map, w_map, prm);

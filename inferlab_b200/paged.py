@@ -185,6 +185,38 @@ class CudaKvPool:
             error)
         return q_out
 
+    def output_project(self, attention: torch.Tensor, weights: torch.Tensor,
+                       residual: torch.Tensor | None = None, out: torch.Tensor | None = None,
+                       stream=None) -> torch.Tensor:
+        """out = residual + attention @ weights.T on the tensor cores
+        (inferlab_cuda_output_project): attention [tokens][in_dim] fp32 or
+        the pool type, weights [out_dim][in_dim] in the pool type, residual /
+        out [tokens][out_dim] fp32."""
+        dev = self.device
+        dtype = TORCH_DTYPES.get(self.dtype)
+        if attention.dtype not in (torch.float32, dtype):
+            raise AttentionError("projection input dtype must be FP32 or the pool dtype")
+        _require(attention, "attention", attention.dtype, dev)
+        _require(weights, "weights", dtype, dev)
+        tokens, in_dim = attention.shape
+        out_dim = weights.shape[0]
+        if weights.shape[1] != in_dim:
+            raise AttentionError("projection shapes do not match")
+        if residual is not None:
+            _require(residual, "residual", torch.float32, dev)
+            if residual.shape != (tokens, out_dim):
+                raise AttentionError("projection shapes do not match")
+        if out is None:
+            out = torch.empty((tokens, out_dim), dtype=torch.float32, device=f"cuda:{dev}")
+        _require(out, "out", torch.float32, dev)
+        a_dtype = KV_FP32 if attention.dtype == torch.float32 else self.dtype
+        error = _lib.error_buffer()
+        _check(self._lib.inferlab_cuda_output_project(
+            self._handle, _vp(attention), a_dtype, _vp(weights),
+            None if residual is None else _vp(residual), tokens, in_dim, out_dim, _vp(out),
+            _stream_handle(dev, stream), error, len(error)), error)
+        return out
+
     def gather(self, block_table: torch.Tensor, tokens: int, stream=None):
         """Contiguous copies [tokens][kv_heads][head_dim] of one sequence's K and V."""
         dev = self.device

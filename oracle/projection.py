@@ -10,7 +10,9 @@ checker for inferlab_cuda_qkv_project_append. Restates:
   * the forward pass's three projections (:1318-1325) as one stacked weight
     [W_q; W_k; W_v];
   * PagedKvPool::append's placement (:713-767): token t's row goes to block
-    table[seq][pos // block_tokens], slot pos % block_tokens.
+    table[seq][pos // block_tokens], slot pos % block_tokens;
+  * the output projection and residual add (:1340-1350): hidden +
+    linear(attention_context, attention_output_weight).
 Pinned: tests/test_projection_oracle.py checks `linear` bit for bit against
 the reference's own function (oracle/_ref/libref_linear.so, built from
 worker/cpp/inferlab_runtime.cpp in place).
@@ -68,3 +70,10 @@ def project_append(hidden: np.ndarray, weights: np.ndarray, q_heads: int, kv_hea
     seq = np.asarray(row_sequences)
     blocks = np.asarray(tables)[seq, pos // block_tokens]
     return q, k, v, blocks, pos % block_tokens
+
+
+def output_project(attention: np.ndarray, weights: np.ndarray, residual=None) -> np.ndarray:
+    """residual + linear(attention, weights), fp32, the reference's order
+    (the residual is added after the full sum, as hidden += attention_output)."""
+    y = linear(attention, weights)
+    return y if residual is None else (np.asarray(residual, np.float32) + y).astype(np.float32)

@@ -97,3 +97,39 @@ def test_projection_rejects_bad_block(torch_mod):
             hidden.float(), weights.float(), 1, torch.zeros(4, dtype=torch.int32, device=dev),
             torch.arange(4, dtype=torch.int32, device=dev), tables)
     pool.close()
+
+
+@pytest.mark.parametrize("dtype,fp32_input", [(2, True), (1, False)])
+def test_output_projection_with_residual(torch_mod, dtype, fp32_input):
+    """out = residual + attention x W_o^T (inferlab_cuda_output_project) against
+    the oracle's fp32 linear fed the same pool-type operands. Products of two
+    16-bit values are exact in fp32, so only the summation order differs:
+    |gpu - ref| <= 1e-4 |ref| + 1e-4 rms(ref)."""
+    torch = torch_mod
+    from inferlab_b200 import CudaKvPool
+    from inferlab_b200 import workloads as wl
+
+    dev = "cuda:0"
+    tdt = wl.TORCH_DTYPES[dtype]
+    pool = CudaKvPool(0, dtype, 4, 16, 1, 32)
+    gen = torch.Generator(device=dev).manual_seed(11 + dtype)
+    tokens, in_dim, out_dim = 200, 512, 352  # ragged token tile, partial feature tile
+    attn = torch.randn((tokens, in_dim), generator=gen, device=dev)
+    if not fp32_input:
+        attn = attn.to(tdt)
+    weights = (torch.randn((out_dim, in_dim), generator=gen, device=dev) / in_dim ** 0.5).to(tdt)
+    residual = torch.randn((tokens, out_dim), generator=gen, device=dev)
+    out = pool.output_project(attn, weights, residual)
+    pool.synchronize()
+    a32 = attn.to(tdt).float().cpu().numpy()
+    ref = projection.output_project(a32, weights.float().cpu().numpy(), residual.cpu().numpy())
+    got = out.cpu().numpy()
+    tol = 1e-4 * np.abs(ref) + 1e-4 * float(np.sqrt(np.mean(ref ** 2)))
+    assert np.all(np.abs(got - ref) <= tol), float(np.max(np.abs(got - ref) - tol))
+    # without a residual
+    out2 = pool.output_project(attn, weights)
+    pool.synchronize()
+    ref2 = projection.output_project(a32, weights.float().cpu().numpy())
+    tol2 = 1e-4 * np.abs(ref2) + 1e-4 * float(np.sqrt(np.mean(ref2 ** 2)))
+    assert np.all(np.abs(out2.cpu().numpy() - ref2) <= tol2)
+    pool.close()
