@@ -133,3 +133,56 @@ def test_output_projection_with_residual(torch_mod, dtype, fp32_input):
     tol2 = 1e-4 * np.abs(ref2) + 1e-4 * float(np.sqrt(np.mean(ref2 ** 2)))
     assert np.all(np.abs(out2.cpu().numpy() - ref2) <= tol2)
     pool.close()
+
+
+def test_attention_layer_chain(torch_mod, oracle_mod):
+    """One prefill chunk through the three device stages a layer needs:
+    inferlab_cuda_qkv_project_append -> inferlab_cuda_paged_prefill ->
+    inferlab_cuda_output_project, each stage checked against its oracle fed
+    the previous stage's device results (projection tolerances as above; the
+    attention stage with the f16/bf16 prefill tolerance 2e-3 |ref| + 1e-3 row
+    max). Two 100-token sequences from position 0, model_dim 256, 4 q / 2 kv
+    heads x 128, bf16."""
+    torch = torch_mod
+    from inferlab_b200 import CudaKvPool
+    from inferlab_b200 import workloads as wl
+
+    from tests.test_gpu_prefill import check_f16
+
+    dev = "cuda:0"
+    pool = CudaKvPool(0, 2, 64, 16, 2, 128)
+    gen = torch.Generator(device=dev).manual_seed(21)
+    tokens, model_dim = 200, 256
+    hidden = torch.randn((tokens, model_dim), generator=gen, device=dev)
+    h16 = hidden.to(torch.bfloat16)
+    w_qkv = (torch.randn(((4 + 4) * 128, model_dim), generator=gen, device=dev) /
+             model_dim ** 0.5).to(torch.bfloat16)
+    w_o = (torch.randn((model_dim, 4 * 128), generator=gen, device=dev) / 512 ** 0.5).to(torch.bfloat16)
+    tables = np.arange(16, dtype=np.int32).reshape(2, 8)
+    seq = np.repeat(np.arange(2, dtype=np.int32), 100)
+    pos = np.tile(np.arange(100, dtype=np.int32), 2)
+    d_tables = torch.from_numpy(tables).to(dev)
+
+    q = pool.project_append(h16, w_qkv, 4, torch.from_numpy(seq).to(dev),
+                            torch.from_numpy(pos).to(dev), d_tables)
+    i32 = lambda a: torch.tensor(a, dtype=torch.int32, device=dev)  # noqa: E731
+    attn = pool.prefill(q, d_tables, i32([0, 0]), i32([100, 100]), i32([0, 100]), 100)
+    out = pool.output_project(attn.view(tokens, -1), w_o, residual=hidden)
+    pool.synchronize()
+
+    # stage 1: projection
+    rq, _, _, _, _ = projection.project_append(h16.float().cpu().numpy(), w_qkv.float().cpu().numpy(),
+                                               4, 2, 128, seq, pos, tables, 16)
+    tol = 2.0 ** -7 * np.abs(rq) + 2.0 ** -8 * float(np.sqrt(np.mean(rq ** 2)))
+    assert np.all(np.abs(q.float().cpu().numpy() - rq) <= tol)
+    # stage 2: attention over the pool the projection filled
+    k_host, v_host = wl.host_arenas(pool)
+    ref_attn = oracle_mod.paged_attention(k_host, v_host, 2, tables, np.array([0, 0]),
+                                          np.array([100, 100]), q.float().cpu().numpy(), 4)
+    check_f16(attn.cpu().numpy(), ref_attn)
+    # stage 3: output projection + residual of the device attention output
+    a16 = attn.view(tokens, -1).to(torch.bfloat16).float().cpu().numpy()
+    ref_out = projection.output_project(a16, w_o.float().cpu().numpy(), hidden.cpu().numpy())
+    tol3 = 1e-4 * np.abs(ref_out) + 1e-4 * float(np.sqrt(np.mean(ref_out ** 2)))
+    assert np.all(np.abs(out.cpu().numpy() - ref_out) <= tol3)
+    pool.close()
