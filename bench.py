@@ -30,7 +30,10 @@ the same tokens from the fp32 attention output).
 (oracle/_ref/libref.so, compiled from kernels/attention_cpu.cpp) on the same
 workload on all host cores: per sequence the page gather plus one
 inferlab_attention_forward call per q-head, as the reference worker's paged
-decode does.
+decode does. With --workload prefill_f16 it times the reference's causal
+attention (Fp16 mode) on one sequence per step, one call per head across the
+host threads; with qkv_append_bf16 / outproj_bf16 the reference's own fp32
+linear (oracle/_ref/libref_linear.so) on a few tokens per host thread.
 """
 from __future__ import annotations
 
@@ -877,9 +880,14 @@ def run_reference(args):
                           "unavailable": "oracle/_ref/libref.so was not built (reference sources "
                                          "absent when the tree was prepared)"}), flush=True)
         return
+    if args.workload == "prefill_f16":
+        return run_reference_prefill(args, world)
+    if args.workload in ("qkv_append_bf16", "outproj_bf16"):
+        return run_reference_projection(args, world)
     if args.workload != "decode_fp32":
         print(json.dumps({"impl": "reference",
-                          "unavailable": f"reference arm implemented for decode_fp32 only"}),
+                          "unavailable": "reference arm implemented for decode_fp32, prefill_f16, "
+                                         "qkv_append_bf16 and outproj_bf16"}),
               flush=True)
         return
     # Host-side copy of the same workload shape (seeded numpy; no GPU on this path).
@@ -927,6 +935,109 @@ def run_reference(args):
         "e2e": {"value": round(value, 4), "unit": "GB/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
+    print(json.dumps(line), flush=True)
+
+
+def _reference_line(args, world, metric, value, unit, workload, threads, sample, dtype):
+    return {
+        "impl": "reference", "metric": metric, "value": round(value, 6), "unit": unit,
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": dtype,
+        "data": "synthetic (seeded)", "config": {"workload": workload},
+        "cpu_baseline": {"value": round(value, 6), "unit": unit, "cores": threads,
+                         "kind": "reference", "sample": sample},
+        "e2e": {"value": round(value, 6), "unit": unit, "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+
+
+def run_reference_prefill(args, world):
+    """The reference's causal prefill on the host: inferlab_attention_forward
+    (OnlineTiled, tile 16, Fp16 storage mode, causal) from oracle/_ref/libref.so,
+    one call per head (heads = 1 on that head's slice) spread over the host
+    threads. Each step is a bounded sample of the 8 x 1024 workload: one
+    sequence, all 16 heads; TFLOP/s counts the same causal FLOPs as our arm."""
+    from concurrent.futures import ThreadPoolExecutor
+
+    from oracle import oracle
+
+    rng = np.random.Generator(np.random.PCG64(2028))
+    tokens, heads, dim = 1024, 16, 128
+    q = (rng.standard_normal((tokens, heads, dim), dtype=np.float32) * 0.5)
+    k = (rng.standard_normal((tokens, heads, dim), dtype=np.float32) * 0.5)
+    v = (rng.standard_normal((tokens, heads, dim), dtype=np.float32) * 0.5)
+    per_head = [(np.ascontiguousarray(q[:, h]), np.ascontiguousarray(k[:, h]),
+                 np.ascontiguousarray(v[:, h])) for h in range(heads)]
+    threads = host_threads()
+
+    def head(h):
+        qh, kh, vh = per_head[h]
+        oracle.attention_forward(qh, kh, vh, tokens, tokens, 1, dim, 0, oracle.ONLINE_TILED,
+                                 oracle.FP16, 16, True, impl="reference")
+
+    flops = 4 * dim * heads * tokens * (tokens + 1) // 2
+    with ThreadPoolExecutor(max_workers=threads) as pool:
+        for _ in range(args.warmup):
+            list(pool.map(head, range(heads)))
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            list(pool.map(head, range(heads)))
+        elapsed = time.perf_counter() - t0
+    value = flops * args.steps / elapsed / 1e12
+    line = _reference_line(
+        args, world, "prefill attn TFLOP/s", value, "TFLOP/s",
+        "causal prefill f16: 8 x 1024 tokens, 16 heads x 128 (reference: one sequence per step)",
+        threads, "each step = one 1024-token sequence, 16 heads, one inferlab_attention_forward "
+                 "call per head (OnlineTiled, tile 16, Fp16 mode) from oracle/_ref/libref.so",
+        "f16")
+    line["ms_per_step"] = round(elapsed / args.steps * 1e3, 4)
+    print(json.dumps(line), flush=True)
+
+
+def run_reference_projection(args, world):
+    """The reference's fp32 linear (worker/cpp/inferlab_runtime.cpp:1266-1285,
+    oracle/_ref/libref_linear.so) over a bounded sample of the projection's
+    tokens: 4 tokens per host thread per step, threads on disjoint rows."""
+    from concurrent.futures import ThreadPoolExecutor
+
+    from oracle import projection
+
+    rng = np.random.Generator(np.random.PCG64(2030))
+    model_dim = 4096
+    outproj = args.workload == "outproj_bf16"
+    in_dim = 32 * 128 if outproj else model_dim
+    out_dim = model_dim if outproj else (32 + 16) * 128
+    w = (rng.standard_normal((out_dim, in_dim), dtype=np.float32) / np.float32(in_dim ** 0.5))
+    threads = host_threads()
+    rows = 4
+    xs = [rng.standard_normal((rows, in_dim), dtype=np.float32) for _ in range(threads)]
+    if projection.ref_linear(xs[0][:1], w[:32]) is None:
+        print(json.dumps({"impl": "reference",
+                          "unavailable": "oracle/_ref/libref_linear.so was not built (reference "
+                                         "sources absent when the tree was prepared)"}), flush=True)
+        return
+
+    def part(i):
+        projection.ref_linear(xs[i], w)
+
+    with ThreadPoolExecutor(max_workers=threads) as pool:
+        for _ in range(args.warmup):
+            list(pool.map(part, range(threads)))
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            list(pool.map(part, range(threads)))
+        elapsed = time.perf_counter() - t0
+    flops = 2.0 * rows * threads * out_dim * in_dim * args.steps
+    value = flops / elapsed / 1e12
+    metric = ("output projection + residual TFLOP/s" if outproj
+              else "qkv projection + paged append TFLOP/s")
+    line = _reference_line(
+        args, world, metric, value, "TFLOP/s",
+        f"{'output' if outproj else 'Q/K/V'} projection {in_dim} -> {out_dim} (reference: "
+        f"{rows * threads} tokens per step)",
+        threads, f"each step = {rows} tokens on each of {threads} threads through the "
+                 f"reference's linear() ({out_dim} x {in_dim} fp32 weights)", "f32")
+    line["ms_per_step"] = round(elapsed / args.steps * 1e3, 4)
     print(json.dumps(line), flush=True)
 
 
