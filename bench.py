@@ -32,8 +32,10 @@ workload on all host cores: per sequence the page gather plus one
 inferlab_attention_forward call per q-head, as the reference worker's paged
 decode does. With --workload prefill_f16 it times the reference's causal
 attention (Fp16 mode) on one sequence per step, one call per head across the
-host threads; with qkv_append_bf16 / outproj_bf16 the reference's own fp32
-linear (oracle/_ref/libref_linear.so) on a few tokens per host thread.
+host threads; with mixed_bf16 the reference worker's per-(sequence, q-head)
+calls for the decode sequences and a 4-of-32-head sample of the chunks; with
+qkv_append_bf16 / outproj_bf16 the reference's own fp32 linear
+(oracle/_ref/libref_linear.so) on a few tokens per host thread.
 """
 from __future__ import annotations
 
@@ -884,10 +886,12 @@ def run_reference(args):
         return run_reference_prefill(args, world)
     if args.workload in ("qkv_append_bf16", "outproj_bf16"):
         return run_reference_projection(args, world)
+    if args.workload == "mixed_bf16":
+        return run_reference_mixed(args, world)
     if args.workload != "decode_fp32":
         print(json.dumps({"impl": "reference",
                           "unavailable": "reference arm implemented for decode_fp32, prefill_f16, "
-                                         "qkv_append_bf16 and outproj_bf16"}),
+                                         "mixed_bf16, qkv_append_bf16 and outproj_bf16"}),
               flush=True)
         return
     # Host-side copy of the same workload shape (seeded numpy; no GPU on this path).
@@ -991,6 +995,73 @@ def run_reference_prefill(args, world):
                  "call per head (OnlineTiled, tile 16, Fp16 mode) from oracle/_ref/libref.so",
         "f16")
     line["ms_per_step"] = round(elapsed / args.steps * 1e3, 4)
+    print(json.dumps(line), flush=True)
+
+
+def run_reference_mixed(args, world):
+    """The reference's continuous-batching step on the host, as its worker runs
+    it: one inferlab_attention_forward call per (sequence, q-head) - the 32
+    decode sequences (contexts from the same seeded clipped Zipf as our arm)
+    in full, and the 4 x 512-token chunks on a sample of 4 of their 32 q-heads,
+    scaled by 8 (their cost is the same for every head). Bf16 storage mode,
+    OnlineTiled, tile 16, causal; calls spread over the host threads. K/V
+    values come from one shared random slice per call (the reference's cost
+    does not depend on them)."""
+    from concurrent.futures import ThreadPoolExecutor
+
+    from inferlab_b200.workloads import zipf_contexts
+    from oracle import oracle
+
+    rng = np.random.Generator(np.random.PCG64(2029))
+    contexts = zipf_contexts(rng, 32)
+    priors = zipf_contexts(rng, 4)
+    chunk, dim, q_heads, sample_heads = 512, 128, 32, 4
+    data = np.random.Generator(np.random.PCG64(7))
+    kmax = int(max(contexts.max(), (priors + chunk).max()))
+    keys = data.standard_normal((kmax, dim), dtype=np.float32)
+    values = data.standard_normal((kmax, dim), dtype=np.float32)
+    q_dec = data.standard_normal((dim,), dtype=np.float32)
+    q_pre = data.standard_normal((chunk, dim), dtype=np.float32)
+    threads = host_threads()
+
+    def decode_call(task):
+        ctx = int(contexts[task // q_heads])
+        oracle.attention_forward(q_dec, keys[:ctx], values[:ctx], 1, ctx, 1, dim, ctx - 1,
+                                 oracle.ONLINE_TILED, oracle.BF16, 16, True, impl="reference")
+
+    def prefill_call(task):
+        prior = int(priors[task // sample_heads])
+        kv = prior + chunk
+        oracle.attention_forward(q_pre, keys[:kv], values[:kv], chunk, kv, 1, dim, prior,
+                                 oracle.ONLINE_TILED, oracle.BF16, 16, True, impl="reference")
+
+    dec_tasks = range(len(contexts) * q_heads)
+    pre_tasks = range(len(priors) * sample_heads)
+    with ThreadPoolExecutor(max_workers=threads) as pool:
+        for _ in range(args.warmup):
+            list(pool.map(decode_call, dec_tasks))
+            list(pool.map(prefill_call, pre_tasks))
+        t_dec = t_pre = 0.0
+        for _ in range(args.steps):
+            t0 = time.perf_counter()
+            list(pool.map(decode_call, dec_tasks))
+            t1 = time.perf_counter()
+            list(pool.map(prefill_call, pre_tasks))
+            t2 = time.perf_counter()
+            t_dec += t1 - t0
+            t_pre += t2 - t1
+    scale = q_heads // sample_heads
+    step_ms = (t_dec + scale * t_pre) / args.steps * 1e3
+    line = _reference_line(
+        args, world, "continuous-batching step ms", step_ms, "ms",
+        "32 decode seqs ctx Zipf(1.1) clip [32,8192] + 4 x 512-token chunked prefill, GQA 32/8 "
+        "x 128 bf16", threads,
+        f"each step = the 32 decode sequences x 32 q-heads in full ({t_dec / args.steps * 1e3:.1f} "
+        f"ms) + the 4 chunks on {sample_heads} of 32 q-heads ({t_pre / args.steps * 1e3:.1f} ms, "
+        f"scaled x{scale}); one inferlab_attention_forward call per (sequence, q-head), Bf16 mode",
+        "bf16")
+    line["higher_is_better"] = False
+    line["ms_per_step"] = round(step_ms, 4)
     print(json.dumps(line), flush=True)
 
 
