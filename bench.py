@@ -34,6 +34,8 @@ decode does. With --workload prefill_f16 it times the reference's causal
 attention (Fp16 mode) on one sequence per step, one call per head across the
 host threads; with mixed_bf16 the reference worker's per-(sequence, q-head)
 calls for the decode sequences and a 4-of-32-head sample of the chunks; with
+longctx_bf16 / longseq_split its paged decode on a sample of the sequences
+or tokens; with
 qkv_append_bf16 / outproj_bf16 the reference's own fp32 linear
 (oracle/_ref/libref_linear.so) on a few tokens per host thread.
 """
@@ -888,10 +890,13 @@ def run_reference(args):
         return run_reference_projection(args, world)
     if args.workload == "mixed_bf16":
         return run_reference_mixed(args, world)
+    if args.workload in ("longctx_bf16", "longseq_split"):
+        return run_reference_long(args, world)
     if args.workload != "decode_fp32":
         print(json.dumps({"impl": "reference",
-                          "unavailable": "reference arm implemented for decode_fp32, prefill_f16, "
-                                         "mixed_bf16, qkv_append_bf16 and outproj_bf16"}),
+                          "unavailable": "reference arm implemented for every workload except "
+                                         "single_seq_fp32, whose line times the reference "
+                                         "itself"}),
               flush=True)
         return
     # Host-side copy of the same workload shape (seeded numpy; no GPU on this path).
@@ -1062,6 +1067,62 @@ def run_reference_mixed(args, world):
         "bf16")
     line["higher_is_better"] = False
     line["ms_per_step"] = round(step_ms, 4)
+    print(json.dumps(line), flush=True)
+
+
+def run_reference_long(args, world):
+    """The reference's paged decode on the host for the long-context lines
+    (GQA 32/8 x 128, bf16 storage): per sequence the page gather plus one
+    inferlab_attention_forward call per q-head (Bf16 mode), the sequences in
+    parallel over the host threads. Bounded samples: longctx_bf16 takes 4 of
+    its 256 sequences per step, longseq_split the first 32,768 of the 131,072
+    tokens (its whole step would hold ~2 GB of widened pages); GB/s counts the
+    same algorithmic bytes as our arm."""
+    from inferlab_b200.workloads import longctx_contexts
+    from oracle import oracle
+
+    longseq = args.workload == "longseq_split"
+    contexts = np.array([32768], np.int64) if longseq else longctx_contexts(2027)[:4]
+    kvh, q_heads, dim = 8, 32, 128
+    need = (contexts + 15) // 16
+    blocks = int(need.sum())
+    rng = np.random.Generator(np.random.PCG64(2031))
+
+    def arena():
+        # bf16 storage bits of values with |x| in [2^-15, 1), random signs
+        bits = rng.integers(0x3800, 0x3F80, size=(blocks, kvh, 16, dim), dtype=np.uint16)
+        return bits | (rng.integers(0, 2, size=bits.shape, dtype=np.uint16) << 15)
+
+    k_arena, v_arena = arena(), arena()
+    perm = rng.permutation(blocks).astype(np.int32)
+    tables = np.zeros((len(contexts), int(need.max())), np.int32)
+    used = 0
+    for i, n in enumerate(need):
+        tables[i, :n] = perm[used:used + n]
+        used += int(n)
+    q = rng.standard_normal((len(contexts), q_heads, dim), dtype=np.float32)
+    bytes_per_step = (int(contexts.sum()) * kvh * dim * 2 * 2 + 2 * len(contexts) * q_heads * dim * 4
+                      + blocks * 4 + len(contexts) * 4)
+    threads = host_threads()
+    for _ in range(args.warmup):
+        oracle.reference_paged_decode_timed(k_arena, v_arena, oracle.BF16, tables, contexts, q,
+                                            q_heads, threads)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        oracle.reference_paged_decode_timed(k_arena, v_arena, oracle.BF16, tables, contexts, q,
+                                            q_heads, threads)
+    elapsed = time.perf_counter() - t0
+    value = bytes_per_step * args.steps / elapsed / 1e9
+    sample = ("the first 32,768 tokens of the one 131,072-token sequence" if longseq
+              else "4 of the 256 sequences (contexts " + ", ".join(str(int(c)) for c in contexts)
+              + ")")
+    line = _reference_line(
+        args, world, "decode attn KV-bytes GB/s", value, "GB/s",
+        ("one 131,072-token sequence, GQA 32/8 x 128 bf16" if longseq
+         else "256 seqs x ctx U[4096, 32768], GQA 32/8 x 128 bf16"), threads,
+        f"each step = {sample}: page gather + one inferlab_attention_forward call per q-head "
+        "(OnlineTiled, tile 16, Bf16 mode) from oracle/_ref/libref.so", "bf16")
+    line["ms_per_step"] = round(elapsed / args.steps * 1e3, 4)
     print(json.dumps(line), flush=True)
 
 

@@ -323,7 +323,9 @@ def reference_paged_decode_timed(k_arena, v_arena, dtype, tables, contexts, q, q
     Per sequence: gather the pages (PagedKvPool::materialize,
     worker/cpp/inferlab_runtime.cpp:769-803) and call the reference's
     inferlab_attention_forward (OnlineTiled) once per q-head on its kv-head
-    slice. ctypes releases the GIL during the call, so the pool runs in parallel.
+    slice. One task per sequence when there are at least as many sequences as
+    threads, else one task per (sequence, q-head) call.
+    ctypes releases the GIL during the call, so the pool runs in parallel.
     Returns the output [num_seqs][q_heads][head_dim].
     """
     lib = ref_lib()
@@ -341,7 +343,7 @@ def reference_paged_decode_timed(k_arena, v_arena, dtype, tables, contexts, q, q
             return blocks.view(np.float16).astype(np.float32)
         return (blocks.astype(np.uint32) << 16).view(np.float32)
 
-    def one(s):
+    def gather(s):
         ctx = int(contexts[s])
         nblk = (ctx + bt - 1) // bt
         ids = tables[s, :nblk]
@@ -349,21 +351,38 @@ def reference_paged_decode_timed(k_arena, v_arena, dtype, tables, contexts, q, q
         vv = widen(v_arena[ids])
         kk = np.ascontiguousarray(kk.transpose(1, 0, 2, 3).reshape(kvh, nblk * bt, hd)[:, :ctx])
         vv = np.ascontiguousarray(vv.transpose(1, 0, 2, 3).reshape(kvh, nblk * bt, hd)[:, :ctx])
+        return kk, vv
+
+    def head(task, kv=None):
+        s, h = divmod(task, q_heads)
+        ctx = int(contexts[s])
+        kk, vv = pages[s] if kv is None else kv
+        kh = kk[h // group]
+        vh = vv[h // group]
+        qh = np.ascontiguousarray(q[s, h])
+        oh = np.zeros(hd, dtype=np.float32)
         err = ctypes.create_string_buffer(512)
         stats = InferlabAttentionStats()
+        status = lib.inferlab_attention_forward(
+            _ptr(qh, ctypes.c_float), _ptr(kh, ctypes.c_float), _ptr(vh, ctypes.c_float),
+            1, ctx, 1, hd, ctx - 1, ctypes.byref(config), _ptr(oh, ctypes.c_float), hd,
+            ctypes.byref(stats), err, 512)
+        if status != 0:
+            raise OracleError(err.value.decode())
+        out[s, h] = oh
+
+    def sequence(s):
+        kv = gather(s)
         for h in range(q_heads):
-            kh = kk[h // group]
-            vh = vv[h // group]
-            qh = np.ascontiguousarray(q[s, h])
-            oh = np.zeros(hd, dtype=np.float32)
-            status = lib.inferlab_attention_forward(
-                _ptr(qh, ctypes.c_float), _ptr(kh, ctypes.c_float), _ptr(vh, ctypes.c_float),
-                1, ctx, 1, hd, ctx - 1, ctypes.byref(config), _ptr(oh, ctypes.c_float), hd,
-                ctypes.byref(stats), err, 512)
-            if status != 0:
-                raise OracleError(err.value.decode())
-            out[s, h] = oh
+            head(s * q_heads + h, kv)
 
     with ThreadPoolExecutor(max_workers=max(1, threads)) as pool:
-        list(pool.map(one, range(len(contexts))))
+        if len(contexts) >= threads:
+            # enough sequences to occupy every thread: one task per sequence
+            list(pool.map(sequence, range(len(contexts))))
+        else:
+            # few long sequences: pages first, then every (sequence, q-head)
+            # call as its own task, so that every thread has work
+            pages = list(pool.map(gather, range(len(contexts))))
+            list(pool.map(head, range(len(contexts) * q_heads)))
     return out
