@@ -179,3 +179,43 @@ def test_pool_api_rejects_bad_arguments_without_gpu():
                                                   1, None, None, 0, err, 256) == -1
     assert err.value == b"paged KV pool pointer is null"
     lib.inferlab_cuda_pool_destroy(None)
+
+
+def test_header_compiles_as_c_and_links(tmp_path):
+    """include/inferlab_attention.h is plain C: a C11 program that includes it,
+    links the library and calls entries whose host-side checks fail before any
+    CUDA work gets the reference's status and messages (no GPU needed)."""
+    from inferlab_b200 import _lib
+
+    src = tmp_path / "main.c"
+    src.write_text(r'''
+#include "inferlab_attention.h"
+#include <stdio.h>
+#include <string.h>
+int main(void) {
+    char err[512];
+    float q[4] = {0}, out[4] = {0};
+    InferlabAttentionStats stats;
+    int rc = inferlab_attention_forward(q, q, q, 1, 1, 1, 4, 0, NULL, out, 4, &stats, err,
+                                        sizeof err);
+    if (rc != -1 || strcmp(err, "attention config or stats pointer is null") != 0) {
+        printf("forward: %d %s\n", rc, err);
+        return 1;
+    }
+    InferlabCudaKvPool* pool = NULL;
+    rc = inferlab_cuda_pool_create(0, 5, 16, 16, 8, 64, &pool, err, sizeof err);
+    if (rc != -1 || pool != NULL) return 2;
+    rc = inferlab_cuda_qkv_project_append(NULL, NULL, NULL, 1, 64, 1, NULL, NULL, NULL, 1, 1,
+                                          NULL, NULL, err, sizeof err);
+    if (rc != -1 || strcmp(err, "paged KV pool pointer is null") != 0) return 3;
+    puts("ok");
+    return 0;
+}
+''')
+    exe = tmp_path / "main"
+    libdir = os.path.dirname(_lib.LIBPATH)
+    subprocess.run(["gcc", "-std=c11", "-Wall", "-Wextra", "-Werror", "-I",
+                    os.path.join(ROOT, "include"), str(src), "-o", str(exe), "-L", libdir,
+                    "-linferlab_attention_cuda", f"-Wl,-rpath,{libdir}"], check=True)
+    run = subprocess.run([str(exe)], capture_output=True, text=True, timeout=120)
+    assert run.returncode == 0 and run.stdout.strip() == "ok", (run.returncode, run.stdout)
