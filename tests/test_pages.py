@@ -118,7 +118,9 @@ def _run_differential(seed: int, pages: int, page_tokens: int, prefix_capacity: 
 
 
 @pytest.mark.parametrize("seed,pages,page_tokens,prefix_capacity", [
-    (1, 12, 4, 3), (2, 6, 2, 2), (3, 40, 16, 0), (4, 9, 3, 8)])
+    (1, 12, 4, 3), (2, 6, 2, 2), (3, 40, 16, 0), (4, 9, 3, 8),
+    (5, 3, 1, 1),    # one-token pages, a single prefix slot, constant exhaustion
+    (6, 20, 7, 5)])  # page size that divides nothing in the token stream
 def test_matches_restated_pool_on_random_operations(seed, pages, page_tokens, prefix_capacity):
     final = _run_differential(seed, pages, page_tokens, prefix_capacity, 400)
     # the seeds reach the interesting paths
