@@ -217,6 +217,18 @@ size_t inferlab_cuda_paged_decode_workspace_size(const InferlabCudaKvPool* pool,
                                                  uint32_t q_heads, uint32_t max_context_len);
 
 /*
+ * Fixes the decode split length of this pool's later decode calls at
+ * blocks_per_split 16-token blocks (1..1024; 0 restores the planner's own
+ * choice, the default). The planner still caps a split at 256 blocks and a
+ * context at 64 splits. A tuning and test setting with no counterpart in the
+ * reference (its decode is one host call per sequence); workspace sizes
+ * follow it, so query inferlab_cuda_paged_decode_workspace_size after
+ * changing it. Not synchronised with decode calls on other host threads.
+ */
+int inferlab_cuda_pool_set_decode_split(InferlabCudaKvPool* pool, uint32_t blocks_per_split,
+                                        char* error, size_t error_capacity);
+
+/*
  * Zeroes the counters at the front of a decode workspace. Needed once per
  * workspace before its first use; the decode kernel leaves them at zero.
  */
@@ -253,11 +265,14 @@ int inferlab_cuda_paged_decode(InferlabCudaKvPool* pool, const float* queries,
  * may not call cudaMalloc once running). No counterpart in the reference,
  * whose decode runs on the host. The split-KV scratch is a 16 MiB array built
  * into the library (held by every GPU that loads it until the process exits);
- * batches needing more scratch than that are rejected with an error naming
- * the size. The call allocates nothing. Calls share the array: two calls whose
- * work overlaps on the GPU race, so serialise them. The first call on a device
- * looks up the array's device address; make it before any stream capture.
- * Arguments as inferlab_cuda_paged_decode.
+ * batches whose split partials need more than that are rejected with an error
+ * naming the size, while batches with one split per sequence need no scratch
+ * at any size. The call allocates nothing. Calls share the array: two calls
+ * whose work overlaps on the GPU race, so serialise them. The first call on a
+ * device that needs scratch looks up the array's device address and caches
+ * it; make it before any stream capture, and do not call this entry after a
+ * device reset (the cached address goes stale). Arguments as
+ * inferlab_cuda_paged_decode.
  */
 int inferlab_cuda_paged_decode_noalloc(InferlabCudaKvPool* pool, const float* queries,
                                        const int32_t* block_tables, uint32_t max_blocks_per_seq,

@@ -101,6 +101,7 @@ SIGNATURES = {
     "inferlab_cuda_paged_decode_workspace_size": (c_sz, [
         c_vp, ctypes.c_uint32, ctypes.c_uint32, ctypes.c_uint32]),
     "inferlab_cuda_paged_decode_workspace_init": (ctypes.c_int, [c_vp, c_sz, c_vp, c_err, c_sz]),
+    "inferlab_cuda_pool_set_decode_split": (ctypes.c_int, [c_vp, ctypes.c_uint32, c_err, c_sz]),
     "inferlab_cuda_paged_decode": (ctypes.c_int, [
         c_vp, c_vp, c_vp, ctypes.c_uint32, c_vp, ctypes.c_uint32, ctypes.c_uint32,
         ctypes.c_uint32, c_vp, c_vp, c_sz, c_vp, c_err, c_sz]),

@@ -6,7 +6,7 @@ Each .cu file under csrc/ compiles to an object in csrc/_build/ (rebuilt when
 it or any header is newer), then one shared library is linked into
 inferlab_b200/lib/. cudart is linked statically, so the library needs only the
 driver at run time. This is the nvcc step a worker/build.rs would run for the
-Rust worker (see INTEGRATION.md).
+Rust worker.
 """
 from __future__ import annotations
 

@@ -11,6 +11,11 @@ namespace ilb {
 std::size_t decode_workspace_bytes(const InferlabCudaKvPool& pool, std::uint32_t num_seqs,
                                    std::uint32_t q_heads, std::uint32_t max_context_len);
 std::size_t decode_counter_bytes(const InferlabCudaKvPool& pool, std::uint32_t num_seqs);
+// Bytes of that workspace the launch actually touches: 0 when no context is
+// split (one split per sequence) or the shape takes the generic kernel, which
+// keeps no partials; otherwise decode_workspace_bytes.
+std::size_t decode_scratch_bytes(const InferlabCudaKvPool& pool, std::uint32_t num_seqs,
+                                 std::uint32_t q_heads, std::uint32_t max_context_len);
 
 // Argument checks of inferlab_cuda_paged_decode (throws std::runtime_error).
 void check_decode_arguments(const InferlabCudaKvPool& pool, const float* queries,

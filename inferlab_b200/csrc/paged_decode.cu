@@ -34,7 +34,6 @@
 
 #include <algorithm>
 #include <cmath>
-#include <cstdlib>
 
 namespace ilb {
 namespace {
@@ -521,13 +520,10 @@ struct DecodePlan {
 };
 
 DecodePlan plan_decode(std::uint32_t num_seqs, std::uint32_t kv_heads,
-                       std::uint32_t max_context_len) {
+                       std::uint32_t max_context_len, std::uint32_t fixed_blocks_per_split) {
     const std::uint32_t max_blocks =
         (max_context_len + kDecodeBlockTokens - 1) / kDecodeBlockTokens;
-    std::uint32_t bps = 0;
-    if (const char* env = std::getenv("INFERLAB_DECODE_BLOCKS_PER_SPLIT")) {
-        bps = static_cast<std::uint32_t>(std::strtoul(env, nullptr, 10));
-    }
+    std::uint32_t bps = fixed_blocks_per_split;
     if (bps == 0) {
         // Aim for about six waves of two CTAs per SM across 148 SMs if every
         // context were max_context_len long, with at least 8 blocks per split
@@ -692,7 +688,8 @@ void run_decode(InferlabCudaKvPool& p, const float* queries, const std::int32_t*
     if (reinterpret_cast<std::uintptr_t>(queries) % 16 != 0) {
         throw std::runtime_error("paged decode queries must be 16-byte aligned");
     }
-    const DecodePlan plan = plan_decode(num_seqs, p.kv_heads, max_context_len);
+    const DecodePlan plan = plan_decode(num_seqs, p.kv_heads, max_context_len,
+                                        p.decode_blocks_per_split);
     const std::size_t need = workspace_bytes_for(num_seqs, q_heads, p.kv_heads, p.head_dim, plan);
     if (plan.max_splits > 1 && (workspace == nullptr || workspace_bytes < need)) {
         throw std::runtime_error("paged decode workspace is too small");
@@ -744,7 +741,18 @@ namespace ilb {
 
 std::size_t decode_workspace_bytes(const InferlabCudaKvPool& pool, std::uint32_t num_seqs,
                                    std::uint32_t q_heads, std::uint32_t max_context_len) {
-    const auto plan = plan_decode(num_seqs, pool.kv_heads, max_context_len);
+    const auto plan = plan_decode(num_seqs, pool.kv_heads, max_context_len,
+                                  pool.decode_blocks_per_split);
+    return workspace_bytes_for(num_seqs, q_heads, pool.kv_heads, pool.head_dim, plan);
+}
+
+std::size_t decode_scratch_bytes(const InferlabCudaKvPool& pool, std::uint32_t num_seqs,
+                                 std::uint32_t q_heads, std::uint32_t max_context_len) {
+    std::size_t smem = 0;
+    if (select_decode(pool, q_heads / pool.kv_heads, smem) == nullptr) return 0;
+    const auto plan = plan_decode(num_seqs, pool.kv_heads, max_context_len,
+                                  pool.decode_blocks_per_split);
+    if (plan.max_splits <= 1) return 0;
     return workspace_bytes_for(num_seqs, q_heads, pool.kv_heads, pool.head_dim, plan);
 }
 
@@ -777,11 +785,24 @@ extern "C" std::size_t inferlab_cuda_paged_decode_workspace_size(const InferlabC
                                                                  std::uint32_t max_context_len) {
     if (pool == nullptr || num_seqs == 0 || q_heads == 0 || max_context_len == 0) return 0;
     try {
-        const auto plan = ilb::plan_decode(num_seqs, pool->kv_heads, max_context_len);
+        const auto plan = ilb::plan_decode(num_seqs, pool->kv_heads, max_context_len,
+                                           pool->decode_blocks_per_split);
         return ilb::workspace_bytes_for(num_seqs, q_heads, pool->kv_heads, pool->head_dim, plan);
     } catch (...) {
         return 0;  // the decode call itself reports why
     }
+}
+
+extern "C" int inferlab_cuda_pool_set_decode_split(InferlabCudaKvPool* pool,
+                                                   std::uint32_t blocks_per_split, char* error,
+                                                   std::size_t error_capacity) {
+    return ilb::protect(error, error_capacity, [&] {
+        auto& p = ilb::checked_pool(pool);
+        if (blocks_per_split > static_cast<std::uint32_t>(ilb::kMaxBlocksPerSplit)) {
+            throw std::runtime_error("paged decode split length must be at most 1024 blocks");
+        }
+        p.decode_blocks_per_split = blocks_per_split;
+    });
 }
 
 extern "C" int inferlab_cuda_paged_decode_workspace_init(void* workspace,

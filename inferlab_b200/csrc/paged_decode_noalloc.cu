@@ -15,9 +15,13 @@
 // contents, so each call first clears the split counters at its front; two
 // calls whose work overlaps on the GPU (different streams, or different
 // host threads on one device) race on the array and must be serialised by
-// the caller. The first call on each device looks up the array's device
-// address (cudaGetSymbolAddress with that device current) and caches it; make
-// that first call before any stream capture.
+// the caller. Batches whose contexts all fit one split need no scratch and
+// never touch the array. The first call on a device that needs scratch looks
+// up the array's device address (cudaGetSymbolAddress with that device
+// current) and caches it for the life of the process; make that first call
+// before any stream capture. A device reset (cudaDeviceReset, or a context
+// torn down and created again on that device) reloads the library's module
+// and leaves the cached address stale, so calls after one are not supported.
 #include "common.cuh"
 #include "internal.cuh"
 #include "pool.cuh"
@@ -68,7 +72,9 @@ extern "C" int inferlab_cuda_paged_decode_noalloc(InferlabCudaKvPool* pool, cons
         check_decode_arguments(p, queries, block_tables, max_blocks_per_seq, context_lens,
                                num_seqs, q_heads, max_context_len);
         if (out == nullptr) throw std::runtime_error("paged decode output pointer is null");
-        const std::size_t need = decode_workspace_bytes(p, num_seqs, q_heads, max_context_len);
+        // Only a batch whose contexts are split across CTAs keeps partials in
+        // scratch; one split per sequence (or the generic kernel) reads none.
+        const std::size_t need = decode_scratch_bytes(p, num_seqs, q_heads, max_context_len);
         if (need > kStaticScratchBytes) {
             throw std::runtime_error(
                 "paged decode batch needs " + std::to_string(need) +
@@ -76,12 +82,16 @@ extern "C" int inferlab_cuda_paged_decode_noalloc(InferlabCudaKvPool* pool, cons
                 "point; use inferlab_cuda_paged_decode with a caller workspace");
         }
         DeviceGuard guard(p.device);
-        void* scratch = scratch_address(p.device);
         auto s = static_cast<cudaStream_t>(stream);
-        // The split counters must start at zero; the rest is written before it is read.
-        cuda_check(cudaMemsetAsync(scratch, 0, decode_counter_bytes(p, num_seqs), s),
-                   "cudaMemsetAsync(decode scratch counters)");
+        void* scratch = nullptr;
+        if (need > 0) {
+            scratch = scratch_address(p.device);
+            // The split counters must start at zero; the rest is written before it is read.
+            cuda_check(cudaMemsetAsync(scratch, 0, decode_counter_bytes(p, num_seqs), s),
+                       "cudaMemsetAsync(decode scratch counters)");
+        }
         launch_paged_decode(p, queries, block_tables, max_blocks_per_seq, context_lens, num_seqs,
-                            q_heads, max_context_len, out, scratch, kStaticScratchBytes, s);
+                            q_heads, max_context_len, out, scratch,
+                            scratch != nullptr ? kStaticScratchBytes : 0, s);
     });
 }

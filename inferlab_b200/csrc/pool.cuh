@@ -31,6 +31,9 @@ struct InferlabCudaKvPool {
     // (next item, CTAs finished) round-robin from kSchedulerSlots pairs that
     // follow the error word; each launch returns its pair to zero on exit.
     std::atomic<std::uint32_t> scheduler_next{0};
+    // Decode split length in 16-token blocks (0: the planner chooses);
+    // inferlab_cuda_pool_set_decode_split sets it.
+    std::uint32_t decode_blocks_per_split = 0;
 };
 
 namespace ilb {

@@ -85,7 +85,7 @@ class CudaKvPool:
         self.arena_bytes = info.arena_bytes
         self._key_ptr = info.key_arena
         self._value_ptr = info.value_arena
-        self._workspace = None
+        self._workspaces: dict = {}
 
     # -- lifetime -----------------------------------------------------------
     def close(self) -> None:
@@ -246,11 +246,29 @@ class CudaKvPool:
             _vp(ws), size, _stream_handle(self.device, stream), error, len(error)), error)
         return ws
 
+    def set_decode_split(self, blocks_per_split: int) -> None:
+        """Fixes later decodes' split length at blocks_per_split 16-token
+        blocks (0: the planner chooses, the default). A tuning and test knob
+        (inferlab_cuda_pool_set_decode_split)."""
+        error = _lib.error_buffer()
+        _check(self._lib.inferlab_cuda_pool_set_decode_split(
+            self._handle, int(blocks_per_split), error, len(error)), error)
+
     def _cached_workspace(self, num_seqs, q_heads, max_context_len, stream):
+        """The pool's own decode workspace, kept per stream: decodes on one
+        stream run in order and may share it, decodes on two streams would race
+        on its split counters and partials. A workspace outgrown on a stream is
+        replaced only after that stream has finished with it (record_stream)."""
         need = self.workspace_size(num_seqs, q_heads, max_context_len)
-        if self._workspace is None or self._workspace.numel() < need:
-            self._workspace = self.make_workspace(num_seqs, q_heads, max_context_len, stream)
-        return self._workspace
+        key = _stream_handle(self.device, stream).value
+        ws = self._workspaces.get(key)
+        if ws is None or ws.numel() < need:
+            if ws is not None:
+                ws.record_stream(stream if stream is not None
+                                 else torch.cuda.current_stream(self.device))
+            ws = self.make_workspace(num_seqs, q_heads, max_context_len, stream)
+            self._workspaces[key] = ws
+        return ws
 
     def decode(self, queries: torch.Tensor, block_tables: torch.Tensor,
                context_lens: torch.Tensor, max_context_len: int | None = None,

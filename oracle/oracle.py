@@ -68,9 +68,15 @@ class InferlabAttentionStats(ctypes.Structure):
 STAT_FIELDS = [name for name, _ in InferlabAttentionStats._fields_]
 
 
-def build() -> None:
-    """Compile liboracle.so (and libref.so when the reference tree exists)."""
-    subprocess.run(["make", "-s", "-C", HERE], check=True)
+def build(reference_root: str | None = None) -> None:
+    """Compile liboracle.so, and the reference's own kernel into _ref/ when
+    reference_root (or the INFERLAB_REFERENCE_ROOT environment variable) names
+    a reference checkout."""
+    root = reference_root or os.environ.get("INFERLAB_REFERENCE_ROOT", "")
+    cmd = ["make", "-s", "-C", HERE]
+    if root:
+        cmd.append(f"REFERENCE_ROOT={root}")
+    subprocess.run(cmd, check=True)
 
 
 def _ptr(array: np.ndarray, ctype):

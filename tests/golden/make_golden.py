@@ -3,7 +3,7 @@
 
 Run where the reference tree is mounted (it is read, never written):
 
-    python tests/golden/make_golden.py [--reference-root /root/reference]
+    python tests/golden/make_golden.py --reference-root <reference checkout>
 
 Writes:
   attention_probe_v012.json  - the reference's retained attention probe
@@ -111,9 +111,10 @@ def cfg1_reference() -> dict:
 
 def main() -> None:
     parser = argparse.ArgumentParser()
-    parser.add_argument("--reference-root", default="/root/reference")
+    parser.add_argument("--reference-root", required=True,
+                        help="root of the reference checkout (read only)")
     args = parser.parse_args()
-    oracle.build()
+    oracle.build(args.reference_root)
     with open(os.path.join(HERE, "attention_probe_v012.json"), "w") as handle:
         json.dump(probe_fixture(args.reference_root), handle)
         handle.write("\n")

@@ -55,15 +55,13 @@ def test_decode_fp32_full_workload(torch_mod, wl, oracle_mod):
     batch.pool.synchronize()
     close(out.cpu().numpy(), oracle_decode(oracle_mod, wl, batch))
     # the split-free path (one split per sequence) agrees too
-    import os
-
-    os.environ["INFERLAB_DECODE_BLOCKS_PER_SPLIT"] = "256"
+    batch.pool.set_decode_split(256)
     try:
         out2 = batch.pool.decode(batch.queries, batch.block_tables, batch.context_lens,
                                  batch.max_context_len, workspace=batch.pool.make_workspace(
                                      64, 8, 2048))
     finally:
-        del os.environ["INFERLAB_DECODE_BLOCKS_PER_SPLIT"]
+        batch.pool.set_decode_split(0)
     batch.pool.synchronize()
     close(out2.cpu().numpy(), out.cpu().numpy())
     batch.pool.close()

@@ -67,20 +67,81 @@ def test_noalloc_decode_matches_workspace_decode(kind):
     pool.close()
 
 
-def test_noalloc_decode_rejects_batches_beyond_its_scratch():
+SCRATCH_BYTES = 16 << 20  # the array built into the library
+
+
+def test_noalloc_decode_rejects_split_batches_beyond_its_scratch():
+    """64 sequences x 64 q-heads over 8 kv-heads x 128 at a 32768-token bound:
+    the contexts split 8 ways and the partials need more than 16 MiB."""
     import torch
 
     assert torch.cuda.is_available(), "this test needs a CUDA device"
     from inferlab_b200 import workloads as wl
 
-    contexts = np.full(64, 32768)
-    batch = wl.decode_batch(0, 305, 1, contexts[:1], 32, 8, 128, wl.KV_BF16,
-                            max_context_len=32768)
-    queries = torch.zeros((4096, 32, 128), dtype=torch.float32, device="cuda:0")
-    tables = torch.zeros((4096, 2048), dtype=torch.int32, device="cuda:0")
-    lens = torch.full((4096,), 32768, dtype=torch.int32, device="cuda:0")
+    batch = wl.decode_batch(0, 305, 1, np.array([16]), 8, 8, 128, wl.KV_BF16,
+                            max_context_len=16)
+    assert batch.pool.workspace_size(64, 64, 32768) > SCRATCH_BYTES
+    queries = torch.zeros((64, 64, 128), dtype=torch.float32, device="cuda:0")
+    tables = torch.zeros((64, 2048), dtype=torch.int32, device="cuda:0")
+    lens = torch.full((64,), 32768, dtype=torch.int32, device="cuda:0")
     out = torch.empty_like(queries)
     status, message = call_noalloc(batch.pool, queries, tables, lens, 32768, out)
     assert status == -1
     assert "bytes of scratch" in message and "16777216" in message
     batch.pool.close()
+
+
+def test_noalloc_decode_single_split_batch_needs_no_scratch():
+    """1024 sequences x 32 q-heads x 128 with contexts <= 512: every context
+    fits one split, so no scratch is read even though a caller workspace for
+    the shape would be larger than the built-in array."""
+    import torch
+
+    assert torch.cuda.is_available(), "this test needs a CUDA device"
+    from inferlab_b200 import workloads as wl
+
+    rng = np.random.Generator(np.random.PCG64(306))
+    contexts = rng.integers(1, 512, size=1024, endpoint=True)
+    batch = wl.decode_batch(0, 306, len(contexts), contexts, 32, 8, 128, wl.KV_BF16,
+                            max_context_len=512)
+    pool = batch.pool
+    assert pool.workspace_size(1024, 32, 512) > SCRATCH_BYTES
+    ref = pool.decode(batch.queries, batch.block_tables, batch.context_lens, 512)
+    pool.synchronize()
+    ref = ref.cpu().numpy()
+    out = torch.full_like(batch.queries, float("nan"))
+    status, message = call_noalloc(pool, batch.queries, batch.block_tables, batch.context_lens,
+                                   512, out)
+    assert status == 0, message
+    pool.synchronize()
+    close(out.cpu().numpy(), ref)
+    pool.close()
+
+
+def test_noalloc_decode_split_batch_just_under_the_limit_twice():
+    """120 sequences x 32 q-heads x 128 at a 32768-token bound split 8 ways:
+    the partials take about 95% of the array. Two calls in a row."""
+    import torch
+
+    assert torch.cuda.is_available(), "this test needs a CUDA device"
+    from inferlab_b200 import workloads as wl
+
+    rng = np.random.Generator(np.random.PCG64(307))
+    contexts = rng.integers(1, 32768, size=120, endpoint=True)
+    contexts[:6] = [32768, 32767, 4097, 4096, 17, 1]
+    batch = wl.decode_batch(0, 307, len(contexts), contexts, 32, 8, 128, wl.KV_BF16,
+                            max_context_len=32768)
+    pool = batch.pool
+    need = pool.workspace_size(120, 32, 32768)
+    assert 0.9 * SCRATCH_BYTES < need <= SCRATCH_BYTES
+    ref = pool.decode(batch.queries, batch.block_tables, batch.context_lens, 32768)
+    pool.synchronize()
+    ref = ref.cpu().numpy()
+    for _ in range(2):
+        out = torch.full_like(batch.queries, float("nan"))
+        status, message = call_noalloc(pool, batch.queries, batch.block_tables,
+                                       batch.context_lens, 32768, out)
+        assert status == 0, message
+        pool.synchronize()
+        close(out.cpu().numpy(), ref)
+    pool.close()
