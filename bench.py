@@ -3,41 +3,38 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--workload NAME] [--impl ours|reference]
 
-Default workload (decode_fp32): paged decode attention, fp32, 64 sequences with
-context ~ U[64, 2048], 8 heads x head_dim 64, 16-token blocks, block tables
-dealt from a seeded permutation of an 8192-block pool, one query token per
-sequence. A step is one decode launch over the whole batch. Metric: decode
-KV-bytes GB/s = algorithmic bytes / kernel time, where algorithmic bytes =
-sum(ctx) * kv_heads * head_dim * 2 * bytes + fp32 queries and outputs + table
-entries and context lengths. With N GPUs every rank runs its own batch (seed
-offset by rank, no collective on the data path) and value = all bytes / max
-rank time ("scaling": "weak").
+Default (no --workload): one JSON line whose headline is the long-context
+paged decode, bf16, GQA 32 q / 8 kv heads x 128: 256 sequences with context
+~ U[4096, 32768] (seed 2027), 16-token blocks, sequences sharded across the
+ranks by a longest-first greedy split of their lengths (no collective; the
+256 sequences are the whole job at every N, "scaling": "strong"). A step is
+one decode launch over the rank's sequences. Metric: decode KV-bytes GB/s =
+algorithmic bytes / kernel time, algorithmic bytes = sum(ctx) * kv_heads *
+head_dim * 2 * element bytes + fp32 queries and outputs + table entries and
+context lengths; value = all ranks' bytes / the slowest rank's time. Beside it,
+each timed in the same run, are the other halves of the metric:
+prefill_f16 (causal prefill 8 x 1024 tokens, 16 heads x 128, f16; TFLOP/s per
+rank, one batch per rank), decode_fp32 (64 sequences x U[64, 2048], 8 heads x
+64, fp32; one batch per rank) and longseq_split (one 131,072-token sequence
+split across the ranks by contiguous block ranges, partials all-gathered over
+NCCL and merged in rank order). Every object carries its roofline, per-rank
+step times and clocks; at N = 1 the CPU baseline legs time the reference's
+own kernel (oracle/_ref/libref.so, built from kernels/attention_cpu.cpp) on a
+bounded sample of the same data and record how its outputs compare with ours.
 
-Other workloads: longctx_bf16 (256 sequences, context U[4096, 32768], GQA
-32/8 x 128, bf16; sequences sharded across ranks, strong scaling), prefill_f16
-(8 x 1024 causal prefill, 16 heads x 128, f16; TFLOP/s), mixed_bf16 (one
-continuous-batching step), longseq_split (one 131,072-token sequence split
-across ranks, NCCL merge), single_seq_fp32 (the drop-in C entry
-inferlab_attention_forward with host buffers on one 129 x 4 x 32 sequence:
-prefill of 128 queries plus one decode query; launch-bound, microseconds per
-call, no roofline claim), qkv_append_bf16 (the Q/K/V projection of the mixed
-step's 4 x 512 chunk tokens, model_dim 4096, with the K/V rows appended to
-the pool in the same launch; TFLOP/s, CPU baseline the reference's own fp32
-linear on one thread), outproj_bf16 (the output projection + residual add of
-the same tokens from the fp32 attention output).
+--workload NAME prints that workload's line alone: longctx_bf16,
+decode_fp32, prefill_f16, longseq_split, mixed_bf16 (one continuous-batching
+step: 32 decode sequences with context Zipf(1.1) clipped to [32, 8192] + 4 x
+512-token prefill chunks, GQA 32/8 x 128 bf16), single_seq_fp32 (the drop-in
+C entry inferlab_attention_forward with host buffers on one 129 x 4 x 32
+sequence: prefill of 128 queries plus one decode query), qkv_append_bf16 and
+outproj_bf16 (the projections either side of attention on the mixed step's
+chunk tokens).
 
---impl reference times the reference's own CPU kernel
-(oracle/_ref/libref.so, compiled from kernels/attention_cpu.cpp) on the same
-workload on all host cores: per sequence the page gather plus one
-inferlab_attention_forward call per q-head, as the reference worker's paged
-decode does. With --workload prefill_f16 it times the reference's causal
-attention (Fp16 mode) on one sequence per step, one call per head across the
-host threads; with mixed_bf16 the reference worker's per-(sequence, q-head)
-calls for the decode sequences and a 4-of-32-head sample of the chunks; with
-longctx_bf16 / longseq_split its paged decode on a sample of the sequences
-or tokens; with
-qkv_append_bf16 / outproj_bf16 the reference's own fp32 linear
-(oracle/_ref/libref_linear.so) on a few tokens per host thread.
+--impl reference times the reference's own CPU kernel on the host cores for
+the same workload (rank 0 only; other ranks exit): per sequence the page
+gather plus one inferlab_attention_forward call per q-head, as the reference
+worker's paged decode does, on a bounded sample of the workload per step.
 """
 from __future__ import annotations
 
@@ -56,6 +53,8 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 L2_FLUSH_BYTES = 256 << 20  # > 126 MB L2
+L2_NOTE = ("flushed between steps: 256 MB write then 256 MB read of a second buffer, outside "
+           "the step events")
 
 
 def load_peaks() -> tuple[dict, str]:
@@ -68,7 +67,8 @@ def load_peaks() -> tuple[dict, str]:
 
 def read_traffic(name: str):
     """DRAM bytes per launch from a committed ncu summary (profiles/<name>.md,
-    line 'traffic_bytes_per_launch: N'), or None."""
+    line 'traffic_bytes_per_launch: N'), or None. The summary records the
+    kernel version it was captured on; the bench does not re-measure it."""
     path = os.path.join(ROOT, "profiles", f"{name}.md")
     if not os.path.exists(path):
         return None
@@ -80,6 +80,14 @@ def read_traffic(name: str):
                 except ValueError:
                     return None
     return None
+
+
+def traffic_fields(name: str) -> dict:
+    value = read_traffic(name)
+    return {"traffic": value,
+            "traffic_source": (f"profiles/{name}.md (ncu dram__bytes_read.sum + "
+                               "dram__bytes_write.sum per launch, committed summary; not "
+                               "measured in this run)") if value is not None else None}
 
 
 class L2Flush:
@@ -143,9 +151,10 @@ class ClockSampler:
             except subprocess.TimeoutExpired:
                 self.proc.kill()
             self.reader.join(timeout=2)
+            self.proc = None
 
     def summary(self) -> dict:
-        sms, maxes, reasons = [], [], set()
+        sms, maxes, power, reasons = [], [], [], set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         for line in self.lines:
             parts = [p.strip() for p in line.split(",")]
@@ -154,6 +163,7 @@ class ClockSampler:
             try:
                 sms.append(float(parts[1]))
                 maxes.append(float(parts[2]))
+                power.append(float(parts[3]))
             except ValueError:
                 continue
             for name, flag in zip(names, parts[5:9]):
@@ -162,6 +172,7 @@ class ClockSampler:
         if not sms:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
         return {"sm_mhz": statistics.median(sms), "sm_max_mhz": max(maxes),
+                "power_w_max": max(power) if power else None,
                 "reasons": sorted(reasons), "samples": len(sms)}
 
 
@@ -213,10 +224,88 @@ def sum_over_ranks(dist, value: float) -> float:
     return float(t.item())
 
 
+def per_rank(dist, **values) -> list[dict]:
+    """Every rank's named numbers (None allowed), gathered in rank order."""
+    keys = sorted(values)
+    row = [float("nan") if values[k] is None else float(values[k]) for k in keys]
+    if dist is None:
+        rows = [row]
+    else:
+        import torch
+
+        t = torch.tensor(row, dtype=torch.float64, device="cuda")
+        parts = [torch.empty_like(t) for _ in range(dist.get_world_size())]
+        dist.all_gather(parts, t)
+        rows = [p.tolist() for p in parts]
+    out = []
+    for rank, r in enumerate(rows):
+        entry = {"rank": rank}
+        for k, v in zip(keys, r):
+            entry[k] = None if v != v else round(v, 5)
+        out.append(entry)
+    return out
+
+
+def host_threads() -> int:
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
+def cpu_model() -> str:
+    try:
+        with open("/proc/cpuinfo") as handle:
+            for line in handle:
+                if line.startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+def timed_region(args, dist, device, stream, flush, parts):
+    """Untimed 0.5 s pre-roll of the step (so the clock samples see the GPU
+    under this load), then exactly args.steps steps, each part bracketed by its
+    own CUDA events on `stream`, with the L2 flushed before every step; a
+    barrier and a device synchronize on both sides. Returns each part's total
+    milliseconds on this rank."""
+    import torch
+
+    preroll_end = time.perf_counter() + 0.5
+    while time.perf_counter() < preroll_end:
+        flush.fill_(0.0)
+        for part in parts:
+            part()
+        stream.synchronize()
+    events = [[(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+               for _ in parts] for _ in range(args.steps)]
+    barrier(dist)
+    torch.cuda.synchronize(device)
+    # Keep the GPU busy while the host enqueues every timed step, so the step
+    # events time the kernels and not the host's launch latency.
+    torch.cuda._sleep(int(2e6 + 3e5 * args.steps))
+    for i in range(args.steps):
+        flush.fill_(float(i))  # evict the previous step's data from L2
+        for (start, end), part in zip(events[i], parts):
+            start.record(stream)
+            part()
+            end.record(stream)
+    torch.cuda.synchronize(device)
+    barrier(dist)
+    return [sum(events[i][k][0].elapsed_time(events[i][k][1]) for i in range(args.steps))
+            for k in range(len(parts))]
+
+
 # ---------------------------------------------------------------------------
-# workloads
+# decode (long-context headline and fp32 sub-line)
 # ---------------------------------------------------------------------------
-def build_decode(workload: str, rank: int, world: int, device: int):
+LONGCTX_SEED = 2027
+LONGCTX_SAMPLE = 4  # sequences the CPU baseline leg takes
+
+
+def build_decode(workload: str, rank: int, world: int, device: int, longctx_seqs: int = 256):
+    from inferlab_b200 import distributed
     from inferlab_b200 import workloads as wl
 
     if workload == "decode_fp32":
@@ -228,48 +317,100 @@ def build_decode(workload: str, rank: int, world: int, device: int):
                 "per_rank": "independent batch per rank"}
         return batch, desc, "f32", "weak"
     if workload == "longctx_bf16":
-        contexts = wl.longctx_contexts(2027)
-        # greedy longest-processing-time split of sequences across ranks
-        order = np.argsort(-contexts, kind="stable")
-        loads = np.zeros(world, np.int64)
-        owner = np.zeros(len(contexts), np.int64)
-        for i in order:
-            r = int(np.argmin(loads))
-            owner[i] = r
-            loads[r] += contexts[i]
+        contexts = wl.longctx_contexts(LONGCTX_SEED)[:longctx_seqs]
+        owner = distributed.shard_sequences(contexts, world)
         mine = contexts[owner == rank]
-        batch = wl.longctx_bf16(device=device, seed=2027 + rank, contexts=mine)
-        desc = {"workload": "paged decode bf16: 256 seqs x ctx U[4096,32768], GQA 32q/8kv x 128, "
-                            "block 16, sequences sharded across GPUs",
-                "num_seqs_total": 256, "num_seqs_this_rank": int(len(mine)), "q_heads": 32,
-                "kv_heads": 8, "head_dim": 128, "block_tokens": 16, "seed": 2027}
+        batch = wl.longctx_bf16(device=device, seed=LONGCTX_SEED + rank, contexts=mine)
+        desc = {"workload": f"paged decode bf16: {len(contexts)} seqs x ctx U[4096,32768], "
+                            "GQA 32q/8kv x 128, block 16, sequences sharded across GPUs",
+                "num_seqs_total": int(len(contexts)), "num_seqs_this_rank": int(len(mine)),
+                "q_heads": 32, "kv_heads": 8, "head_dim": 128, "block_tokens": 16,
+                "seed": LONGCTX_SEED, "sum_context_total": int(contexts.sum()),
+                "sharding": "longest-first greedy over context lengths, no collective"}
         return batch, desc, "bf16", "strong"
     raise SystemExit(f"unknown decode workload {workload}")
 
 
-def run_ours(args):
+def host_sample(pool, tables_host, contexts, seqs):
+    """Host copies of the blocks of sequences `seqs` (compacted) and their
+    tables renumbered into the copy."""
     import torch
 
-    from inferlab_b200 import _lib
+    need = (np.asarray(contexts)[seqs] + 15) // 16
+    ids = np.unique(np.concatenate([tables_host[s, :n] for s, n in zip(seqs, need)]))
+    index = torch.from_numpy(ids.astype(np.int64)).to(f"cuda:{pool.device}")
 
-    world, rank, local = dist_env()
-    dist = init_dist(world, local)
-    device = local
-    peaks, peak_kind = load_peaks()
-    _lib.lib()  # fails loudly if the CUDA library is missing
+    def grab(arena):
+        part = arena.index_select(0, index)
+        if part.dtype == torch.float32:
+            return part.cpu().numpy()
+        return part.view(torch.int16).cpu().numpy().view(np.uint16)
 
-    if args.workload == "prefill_f16":
-        return run_prefill(args, dist, world, rank, device, peaks, peak_kind)
-    if args.workload == "mixed_bf16":
-        return run_mixed(args, dist, world, rank, device, peaks, peak_kind)
-    if args.workload in ("qkv_append_bf16", "outproj_bf16"):
-        return run_projection(args, dist, world, rank, device, peaks, peak_kind)
-    if args.workload == "single_seq_fp32":
-        return run_single_sequence(args, dist, world, rank, device)
-    if args.workload == "longseq_split":
-        return run_long_sequence(args, dist, world, rank, device, peaks, peak_kind)
+    remap = np.zeros(pool.num_blocks, np.int64)
+    remap[ids] = np.arange(len(ids))
+    width = int(need.max())
+    tables = np.zeros((len(seqs), width), np.int32)
+    for i, (s, n) in enumerate(zip(seqs, need)):
+        tables[i, :n] = remap[tables_host[s, :n]]
+    return grab(pool.key_arena), grab(pool.value_arena), tables
 
-    batch, desc, dtype_name, scaling = build_decode(args.workload, rank, world, device)
+
+def compare(got, ref, rtol, atol=0.0, row_atol=0.0) -> dict:
+    got = np.asarray(got, np.float64)
+    ref = np.asarray(ref, np.float64)
+    err = np.abs(got - ref)
+    row = np.max(np.abs(ref), axis=-1, keepdims=True)
+    big = np.abs(ref) > 1e-2
+    bound = atol + rtol * np.abs(ref) + row_atol * row
+    return {"max_abs": float(err.max()),
+            "max_rel_ref_gt_1e-2": float((err[big] / np.abs(ref[big])).max()) if big.any() else 0.0,
+            "max_err_over_rowmax": float(np.max(err / np.maximum(row, 1e-30))),
+            "within_tolerance": bool(np.all(err <= bound)),
+            "elements": int(err.size)}
+
+
+def cpu_baseline_decode(sample, bytes_per_step_sample, q_heads, dtype, seconds, what):
+    """The reference CPU kernel (page gather + one inferlab_attention_forward
+    per q-head, OnlineTiled tile 16) on a host sample of the timed workload,
+    on all host threads, repeated for about `seconds`; plus one single-thread
+    pass over its first sequence, and how its outputs compare with ours."""
+    from oracle import oracle
+
+    k_host, v_host, tables, contexts, q, ours = sample
+    threads = host_threads()
+    steps = 0
+    ref = None
+    t0 = time.perf_counter()
+    while True:
+        ref = oracle.reference_paged_decode_timed(k_host, v_host, dtype, tables, contexts, q,
+                                                  q_heads, threads)
+        steps += 1
+        elapsed = time.perf_counter() - t0
+        if elapsed >= seconds:
+            break
+    kind = "reference" if oracle.ref_lib() is not None else "port"
+    first = np.array([contexts[0]])
+    one_bytes = bytes_per_step_sample * float(contexts[0]) / float(np.sum(contexts))
+    t1 = time.perf_counter()
+    oracle.reference_paged_decode_timed(k_host, v_host, dtype, tables[:1], first, q[:1], q_heads, 1)
+    single = one_bytes / (time.perf_counter() - t1) / 1e9
+    parity = compare(ours, ref, rtol=1e-5, atol=1e-6)
+    parity["tolerance"] = "|ours - reference| <= 1e-6 + 1e-5 |reference| (fp32 arithmetic)"
+    return {"value": round(bytes_per_step_sample * steps / elapsed / 1e9, 4), "unit": "GB/s",
+            "cores": threads, "kind": kind, "cpu_model": cpu_model(),
+            "single_thread_value": round(single, 4),
+            "sample": f"{what}: {steps} passes in {elapsed:.1f} s; page gather + "
+                      "inferlab_attention_forward (OnlineTiled, tile 16) per q-head from "
+                      "oracle/_ref/libref.so, sequences (or (sequence, q-head) calls) spread "
+                      "over the host threads",
+            "parity_sample": parity}
+
+
+def measure_decode(args, dist, world, rank, device, peaks, peak_kind, workload):
+    import torch
+
+    batch, desc, dtype_name, scaling = build_decode(workload, rank, world, device,
+                                                    args.longctx_seqs)
     pool = batch.pool
     stream = torch.cuda.current_stream(device)
     num_seqs = len(batch.contexts)
@@ -286,50 +427,40 @@ def run_ours(args):
         flush.fill_(float(i))
         step()
     pool.synchronize()
-    # Clock samples: a ~0.5 s untimed pre-roll of the same step, the timed
-    # steps and the e2e steps (the timed region alone is a few milliseconds,
-    # shorter than nvidia-smi's sampling interval).
     clocks = ClockSampler(device).__enter__()
-    preroll_end = time.perf_counter() + 0.5
-    while time.perf_counter() < preroll_end:
-        flush.fill_(0.0)
-        step()
-        stream.synchronize()
-
-    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    barrier(dist)
-    torch.cuda.synchronize(device)
-    wall0 = time.perf_counter()
-    # Keep the GPU busy while the host enqueues every timed step, so the step
-    # events time the kernels and not the host's launch latency.
-    torch.cuda._sleep(int(2e6 + 3e5 * args.steps))
-    for i in range(args.steps):
-        flush.fill_(float(i))  # evict the previous step's K/V from L2
-        starts[i].record(stream)
-        step()
-        ends[i].record(stream)
-    torch.cuda.synchronize(device)
-    wall = time.perf_counter() - wall0
-    barrier(dist)
+    (kernel_ms,) = timed_region(args, dist, device, stream, flush, [step])
     pool.synchronize()
-    kernel_ms = sum(s.elapsed_time(e) for s, e in zip(starts, ends))
     total_ms = max_over_ranks(dist, kernel_ms)
     all_bytes = sum_over_ranks(dist, float(bytes_per_step) * args.steps)
     value = all_bytes / (total_ms * 1e-3) / 1e9
-    ms_per_step = total_ms / args.steps
     achieved = bytes_per_step / (kernel_ms / args.steps * 1e-3) / 1e9
     peak = float(peaks["hbm_gbs"])
 
-    e2e = run_decode_e2e(args, batch, pool, workspace, flush, device, dist, bytes_per_step)
+    # CPU baseline sample (rank 0, one GPU): copied before the end-to-end steps
+    # append new rows to the pool.
+    sample = None
+    want_cpu = rank == 0 and world == 1 and not args.no_cpu_baseline
+    if want_cpu:
+        from inferlab_b200 import workloads as wl
+
+        seqs = (list(range(num_seqs)) if workload == "decode_fp32"
+                else list(range(min(LONGCTX_SAMPLE, num_seqs))))
+        k_host, v_host, tables = host_sample(pool, batch.tables_host, batch.contexts, seqs)
+        q = wl.round_queries(batch.queries, pool.dtype)[seqs]
+        sample = (k_host, v_host, tables, batch.contexts[seqs], q, out.cpu().numpy()[seqs])
+        ctx = batch.contexts[seqs].astype(np.int64)
+        sample_bytes = (int(ctx.sum()) * batch.kv_heads * batch.head_dim * 2 * pool.element_bytes
+                        + 2 * len(seqs) * batch.q_heads * batch.head_dim * 4
+                        + int(((ctx + 15) // 16).sum()) * 4 + len(seqs) * 4)
+
+    e2e = run_decode_e2e(args, batch, pool, flush, device, dist, bytes_per_step)
     clocks.__exit__(None, None, None)
-
-    cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        cpu = cpu_baseline_decode(batch, bytes_per_step, args.cpu_seconds)
-
     clock = clocks.summary()
     clock["window"] = "0.5 s pre-roll of the same step + timed steps + e2e steps"
+    ranks = per_rank(dist, ms_per_step=kernel_ms / args.steps, sm_mhz=clock["sm_mhz"],
+                     e2e_ms_per_step=e2e["rank_ms_per_step"], gbs=achieved)
+    e2e.pop("rank_ms_per_step")
+    profile = f"paged_decode_{workload}"
     line = {
         "metric": "decode attn KV-bytes GB/s",
         "value": round(value, 3),
@@ -337,34 +468,36 @@ def run_ours(args):
         "n_gpus": world,
         "steps": args.steps,
         "warmup": args.warmup,
-        "ms_per_step": round(ms_per_step, 5),
+        "ms_per_step": round(total_ms / args.steps, 5),
         "higher_is_better": True,
         "scaling": scaling,
         "vs_baseline": None,
         "dtype": dtype_name,
         "data": "synthetic (seeded N(0,1) Q/K/V, seeded contexts and block tables)",
-        "config": dict(desc, l2="flushed between steps: 256 MB write then 256 MB read of a second "
-                                "buffer, outside the step events",
-                       parallelism=f"sequence-sharded x{world}, no collective"),
-        "roofline": {"bound": "hbm", "achieved": round(achieved, 2), "peak": peak, "unit": "GB/s",
-                     "frac": round(achieved / peak, 4), "peak_kind": f"{peak_kind} hbm_gbs",
-                     "traffic": read_traffic(f"paged_decode_{args.workload}"),
-                     "algorithmic_bytes_per_launch": int(bytes_per_step)},
+        "config": dict(desc, l2=L2_NOTE, parallelism=f"sequence-sharded x{world}, no collective"),
+        "roofline": dict({"bound": "hbm", "achieved": round(achieved, 2), "peak": peak,
+                          "unit": "GB/s", "frac": round(achieved / peak, 4),
+                          "peak_kind": f"{peak_kind} hbm_gbs",
+                          "algorithmic_bytes_per_launch": int(bytes_per_step),
+                          "rank": rank}, **traffic_fields(profile)),
         "e2e": e2e,
         "gpu_launches": args.steps,
         "clocks": clock,
-        "wall_s_timed_region": round(wall, 4),
+        "per_rank": ranks,
     }
-    if cpu is not None:
-        line["cpu_baseline"] = cpu
     pool.close()
-    if rank == 0:
-        print(json.dumps(line), flush=True)
-    if dist is not None:
-        dist.destroy_process_group()
+    del workspace, out, flush
+    torch.cuda.empty_cache()
+    if sample is not None:
+        what = ("the whole 64-sequence batch" if workload == "decode_fp32" else
+                f"{len(sample[3])} of the 256 sequences (contexts "
+                + ", ".join(str(int(c)) for c in sample[3]) + ")")
+        line["cpu_baseline"] = cpu_baseline_decode(sample, sample_bytes, batch.q_heads,
+                                                   batch.pool.dtype, args.cpu_seconds, what)
+    return line
 
 
-def run_decode_e2e(args, batch, pool, workspace, flush, device, dist, bytes_per_step):
+def run_decode_e2e(args, batch, pool, flush, device, dist, bytes_per_step):
     """The same decode step through the C ABI with HOST buffers: one
     inferlab_cuda_decode_step_host call per step takes the step's queries,
     the new token's K/V rows, the block tables and context lengths from host
@@ -413,35 +546,249 @@ def run_decode_e2e(args, batch, pool, workspace, flush, device, dist, bytes_per_
         total += time.perf_counter() - t0
     pool.synchronize()
     barrier(dist)
+    mine = total
     total = max_over_ranks(dist, total)
     all_bytes = sum_over_ranks(dist, float(bytes_per_step) * args.steps)
     return {"value": round(all_bytes / total / 1e9, 3), "unit": "GB/s",
             "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
             "ms_per_step": round(total / args.steps * 1e3, 5),
+            "rank_ms_per_step": mine / args.steps * 1e3,
             "gpu_launches_per_step": 2,
             "path": "inferlab_cuda_decode_step_host with page-locked host arrays: a prologue "
                     "kernel reads them over the bus (appends the new K/V rows, stages q, "
                     "tables and lengths in HBM), the paged decode writes the output straight "
                     "into the host array, a 4-byte copy returns the error word; host wall "
-                    "clock per call"}
+                    "clock per call, max over ranks"}
 
 
-def host_threads() -> int:
+# ---------------------------------------------------------------------------
+# prefill
+# ---------------------------------------------------------------------------
+def cpu_baseline_prefill(pool, batch, ours, seconds):
+    """The reference's causal prefill on the host on segment 0 of the timed
+    batch (1024 tokens, all 16 heads): inferlab_attention_forward (OnlineTiled,
+    tile 16, Fp16 storage mode, causal) from oracle/_ref/libref.so, one call
+    per head (heads = 1 on that head's slice of the pool's f16 K/V and the
+    f16 queries), the heads spread over the host threads; repeated for about
+    `seconds`. Also how the reference's outputs compare with ours."""
+    from concurrent.futures import ThreadPoolExecutor
+
+    from oracle import oracle
+
+    tokens = int(batch.counts[0])
+    heads, dim = batch.q_heads, batch.head_dim
+    k_host, v_host, tables = host_sample(pool, batch.prefill_tables_host,
+                                         batch.starts + batch.counts, [0])
+    nblk = (tokens + 15) // 16
+    ids = tables[0, :nblk]
+
+    def widen(bits):  # [nblk][kvh][16][dim] f16 bits -> [kvh][tokens][dim] fp32
+        x = bits[ids].view(np.float16).astype(np.float32)
+        return x.transpose(1, 0, 2, 3).reshape(x.shape[1], nblk * 16, dim)[:, :tokens]
+
+    kk, vv = widen(k_host), widen(v_host)
+    q = batch.prefill_queries[:tokens].float().cpu().numpy()  # [tokens][heads][dim]
+    group = heads // kk.shape[0]
+    per_head = [(np.ascontiguousarray(q[:, h]), np.ascontiguousarray(kk[h // group]),
+                 np.ascontiguousarray(vv[h // group])) for h in range(heads)]
+    ref = np.zeros((tokens, heads, dim), np.float32)
+
+    def head(h):
+        qh, kh, vh = per_head[h]
+        o, _ = oracle.attention_forward(qh, kh, vh, tokens, tokens, 1, dim, 0,
+                                        oracle.ONLINE_TILED, oracle.FP16, 16, True,
+                                        impl="reference")
+        ref[:, h] = o.reshape(tokens, dim)
+
+    threads = host_threads()
+    flops = 4 * dim * heads * tokens * (tokens + 1) // 2
+    passes = 0
+    with ThreadPoolExecutor(max_workers=threads) as ex:
+        t0 = time.perf_counter()
+        while True:
+            list(ex.map(head, range(heads)))
+            passes += 1
+            elapsed = time.perf_counter() - t0
+            if elapsed >= seconds:
+                break
+    parity = compare(ours[:tokens], ref, rtol=2e-3, row_atol=1e-3)
+    parity["tolerance"] = ("|ours - reference| <= 2e-3 |reference| + 1e-3 max|reference row| "
+                           "(fp16 probabilities on the tensor cores); reference in its Fp16 "
+                           "storage mode")
+    return {"value": round(flops * passes / elapsed / 1e12, 6), "unit": "TFLOP/s",
+            "cores": threads, "kind": "reference", "cpu_model": cpu_model(),
+            "sample": f"segment 0 of the batch (1024 tokens, 16 heads): {passes} passes in "
+                      f"{elapsed:.1f} s, one inferlab_attention_forward call per head "
+                      "(OnlineTiled, tile 16, Fp16 mode) from oracle/_ref/libref.so",
+            "parity_sample": parity}
+
+
+def measure_prefill(args, dist, world, rank, device, peaks, peak_kind):
+    import torch
+
+    from inferlab_b200 import workloads as wl
+
+    batch = wl.prefill_f16(device=device, seed=2028 + rank)
+    pool = batch.pool
+    stream = torch.cuda.current_stream(device)
+    flops = batch.prefill_flops()
+    out = torch.empty((batch.prefill_queries.shape[0], batch.q_heads, batch.head_dim),
+                      dtype=torch.float32, device=f"cuda:{device}")
+    flush = L2Flush(device)
+
+    def step():
+        pool.prefill(batch.prefill_queries, batch.prefill_tables, batch.starts_dev,
+                     batch.counts_dev, batch.offsets_dev, int(batch.counts.max()), out=out)
+
+    for i in range(args.warmup):
+        flush.fill_(float(i))
+        step()
+    pool.synchronize()
+    with ClockSampler(device) as clocks:
+        (kernel_ms,) = timed_region(args, dist, device, stream, flush, [step])
+    pool.synchronize()
+    total_ms = max_over_ranks(dist, kernel_ms)
+    all_flops = sum_over_ranks(dist, float(flops) * args.steps)
+    value = all_flops / (total_ms * 1e-3) / 1e12
+    achieved = flops / (kernel_ms / args.steps * 1e-3) / 1e12
+    peak = float(peaks["bf16_tflops"])
+    clock = clocks.summary()
+    line = {
+        "metric": "prefill attn TFLOP/s", "value": round(value, 3), "unit": "TFLOP/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(total_ms / args.steps, 5), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f16",
+        "data": "synthetic (seeded N(0, 0.5^2))",
+        "config": {"workload": "causal prefill f16: 8 x 1024 tokens, 16 heads x 128, paged "
+                               "block 16 (one batch per rank)", "flops_per_step": int(flops),
+                   "flops_counted": "4 * head_dim * score elements (the reference's causal "
+                                    "count, kernels/attention_cpu.cpp:149-168)",
+                   "l2": L2_NOTE},
+        "roofline": dict({"bound": "tensor", "achieved": round(achieved, 2), "peak": peak,
+                          "unit": "TFLOP/s", "frac": round(achieved / peak, 4),
+                          "peak_kind": f"{peak_kind} bf16_tflops (burst; dense f16 = bf16 rate)",
+                          "frac_of_sustained": round(achieved / float(
+                              peaks.get("bf16_tflops_sustained", peak)), 4),
+                          "rank": rank}, **traffic_fields("paged_prefill_prefill_f16")),
+        "gpu_launches": args.steps, "clocks": clock,
+        "per_rank": per_rank(dist, ms_per_step=kernel_ms / args.steps, sm_mhz=clock["sm_mhz"],
+                             tflops=achieved),
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline_prefill(pool, batch, out.cpu().numpy(),
+                                                    min(args.cpu_seconds, 8.0))
+    pool.close()
+    return line
+
+
+# ---------------------------------------------------------------------------
+# one long sequence split across the ranks
+# ---------------------------------------------------------------------------
+def measure_long_sequence(args, dist, world, rank, device, peaks, peak_kind):
+    """One 131072-token sequence split across the ranks: per step, decode
+    partials over the local blocks into one packed [m | l | o] block, one NCCL
+    all-gather of the blocks, rank-order log-sum-exp merge. Timed per rank with
+    events, max over ranks."""
+    import torch
+
+    from inferlab_b200 import distributed, workloads as wl
+
+    batch = wl.long_sequence_shard(device, rank, world)
+    pool = batch.pool
+    stream = torch.cuda.current_stream(device)
+    flush = L2Flush(device)
+    local = int(batch.contexts[0])
+    workspace = pool.make_workspace(1, 32, local)
+
+    def step():
+        return distributed.decode_split_sequence(pool, batch.queries, batch.block_tables, local,
+                                                 workspace=workspace)
+
+    for i in range(args.warmup):
+        flush.fill_(float(i))
+        step()
+    pool.synchronize()
+    with ClockSampler(device) as clocks:
+        (ms,) = timed_region(args, dist, device, stream, flush, [step])
+    pool.synchronize()
+    total_ms = max_over_ranks(dist, ms)
+    kv_bytes = 131072 * 8 * 128 * 2 * 2
+    value = kv_bytes * args.steps / (total_ms * 1e-3) / 1e9
+    clock = clocks.summary()
+    comm = None
+    if dist is not None:
+        comm = dist.get_world_size()
+    line = {
+        "metric": "long-sequence decode KV-bytes GB/s", "value": round(value, 3), "unit": "GB/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(total_ms / args.steps, 5), "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded)",
+        "config": {"workload": "one 131072-token sequence, GQA 32/8 x 128 bf16, blocks split "
+                               "across GPUs, NCCL all-gather of (m, l, o) + rank-order merge",
+                   "tokens_this_rank": local, "comm_nranks": comm,
+                   "collective": ("all_gather_into_tensor over NCCL, "
+                                  f"{32 * 130 * 4} B per rank" if comm else "none (one GPU)"),
+                   "l2": L2_NOTE},
+        "roofline": {"bound": "hbm", "achieved_per_gpu": round(value / world, 2),
+                     "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                     "frac": round(value / world / peaks["hbm_gbs"], 4),
+                     "peak_kind": f"{peak_kind} hbm_gbs"},
+        "gpu_launches": (3 if world > 1 else 2) * args.steps, "clocks": clock,
+        "per_rank": per_rank(dist, ms_per_step=ms / args.steps, sm_mhz=clock["sm_mhz"]),
+    }
+    pool.close()
+    return line
+
+
+# ---------------------------------------------------------------------------
+# default line and dispatch
+# ---------------------------------------------------------------------------
+def run_default(args, dist, world, rank, device, peaks, peak_kind):
+    """The headline long-context decode plus the other halves of the metric,
+    each measured in this run (the same collective steps on every rank)."""
+    line = measure_decode(args, dist, world, rank, device, peaks, peak_kind, "longctx_bf16")
+    line["prefill_f16"] = measure_prefill(args, dist, world, rank, device, peaks, peak_kind)
+    line["decode_fp32"] = measure_decode(args, dist, world, rank, device, peaks, peak_kind,
+                                         "decode_fp32")
+    line["longseq_split"] = measure_long_sequence(args, dist, world, rank, device, peaks,
+                                                  peak_kind)
+    return line
+
+
+def run_ours(args):
+    import torch
+
+    from inferlab_b200 import _lib
+
+    world, rank, local = dist_env()
+    dist = init_dist(world, local)
+    device = local
+    peaks, peak_kind = load_peaks()
+    _lib.lib()  # fails loudly if the CUDA library is missing
     try:
-        return len(os.sched_getaffinity(0))
-    except AttributeError:
-        return os.cpu_count() or 1
-
-
-def cpu_model() -> str:
-    try:
-        with open("/proc/cpuinfo") as handle:
-            for line in handle:
-                if line.startswith("model name"):
-                    return line.split(":", 1)[1].strip()
-    except OSError:
-        pass
-    return "unknown"
+        if args.workload == "default":
+            line = run_default(args, dist, world, rank, device, peaks, peak_kind)
+        elif args.workload in ("longctx_bf16", "decode_fp32"):
+            line = measure_decode(args, dist, world, rank, device, peaks, peak_kind,
+                                  args.workload)
+        elif args.workload == "prefill_f16":
+            line = measure_prefill(args, dist, world, rank, device, peaks, peak_kind)
+        elif args.workload == "longseq_split":
+            line = measure_long_sequence(args, dist, world, rank, device, peaks, peak_kind)
+        elif args.workload == "mixed_bf16":
+            line = run_mixed(args, dist, world, rank, device, peaks, peak_kind)
+        elif args.workload in ("qkv_append_bf16", "outproj_bf16"):
+            line = run_projection(args, dist, world, rank, device, peaks, peak_kind)
+        elif args.workload == "single_seq_fp32":
+            line = run_single_sequence(args, dist, world, rank, device)
+        else:
+            raise SystemExit(f"unknown workload {args.workload}")
+        if rank == 0 and line is not None:
+            print(json.dumps(line), flush=True)
+    finally:
+        if dist is not None:
+            torch.cuda.synchronize(device)
+            dist.destroy_process_group()
 
 
 def run_single_sequence(args, dist, world, rank, device):
@@ -503,109 +850,8 @@ def run_single_sequence(args, dist, world, rank, device):
                                 "cores": 1, "kind": "reference", "cpu_model": cpu_model(),
                                 "sample": "the same two calls on oracle/_ref/libref.so "
                                           "(kernels/attention_cpu.cpp), one thread"}
-    if rank == 0:
-        print(json.dumps(line), flush=True)
+    return line
 
-
-def cpu_baseline_decode(batch, bytes_per_step, seconds: float) -> dict:
-    """The reference CPU kernel on the same pool contents, all host threads."""
-    from inferlab_b200 import workloads as wl
-    from oracle import oracle
-
-    k_host, v_host = wl.host_arenas(batch.pool)
-    q = wl.round_queries(batch.queries, batch.pool.dtype)
-    threads = host_threads()
-    sample = len(batch.contexts)
-    steps = 0
-    t0 = time.perf_counter()
-    while True:
-        oracle.reference_paged_decode_timed(k_host, v_host, batch.pool.dtype, batch.tables_host,
-                                            batch.contexts, q, batch.q_heads, threads)
-        steps += 1
-        elapsed = time.perf_counter() - t0
-        if elapsed >= seconds:
-            break
-    kind = "reference" if oracle.ref_lib() is not None else "port"
-    # single-thread rate on one pass of the same batch
-    t1 = time.perf_counter()
-    oracle.reference_paged_decode_timed(k_host, v_host, batch.pool.dtype, batch.tables_host,
-                                        batch.contexts, q, batch.q_heads, 1)
-    single = bytes_per_step / (time.perf_counter() - t1) / 1e9
-    return {"value": round(bytes_per_step * steps / elapsed / 1e9, 4), "unit": "GB/s",
-            "cores": threads, "kind": kind, "cpu_model": cpu_model(),
-            "single_thread_value": round(single, 4),
-            "sample": f"{steps} full steps ({sample} sequences each) in {elapsed:.1f} s: page gather "
-                      "+ inferlab_attention_forward (OnlineTiled, tile 16) per q-head, "
-                      "oracle/_ref/libref.so built from kernels/attention_cpu.cpp"}
-
-
-def run_prefill(args, dist, world, rank, device, peaks, peak_kind):
-    import torch
-
-    from inferlab_b200 import workloads as wl
-
-    batch = wl.prefill_f16(device=device, seed=2028 + rank)
-    pool = batch.pool
-    stream = torch.cuda.current_stream(device)
-    flops = batch.prefill_flops()
-    out = torch.empty((batch.prefill_queries.shape[0], batch.q_heads, batch.head_dim),
-                      dtype=torch.float32, device=f"cuda:{device}")
-    flush = L2Flush(device)
-
-    def step():
-        pool.prefill(batch.prefill_queries, batch.prefill_tables, batch.starts_dev,
-                     batch.counts_dev, batch.offsets_dev, int(batch.counts.max()), out=out)
-
-    for i in range(args.warmup):
-        flush.fill_(float(i))
-        step()
-    pool.synchronize()
-    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    barrier(dist)
-    torch.cuda.synchronize(device)
-    with ClockSampler(device) as clocks:
-        preroll_end = time.perf_counter() + 0.5
-        while time.perf_counter() < preroll_end:
-            flush.fill_(0.0)
-            step()
-            stream.synchronize()
-        torch.cuda._sleep(int(2e6 + 3e5 * args.steps))
-        for i in range(args.steps):
-            flush.fill_(float(i))
-            starts[i].record(stream)
-            step()
-            ends[i].record(stream)
-        torch.cuda.synchronize(device)
-        barrier(dist)
-    pool.synchronize()
-    kernel_ms = sum(s.elapsed_time(e) for s, e in zip(starts, ends))
-    total_ms = max_over_ranks(dist, kernel_ms)
-    all_flops = sum_over_ranks(dist, float(flops) * args.steps)
-    value = all_flops / (total_ms * 1e-3) / 1e12
-    achieved = flops / (kernel_ms / args.steps * 1e-3) / 1e12
-    peak = float(peaks["bf16_tflops"])
-    line = {
-        "metric": "prefill attn TFLOP/s", "value": round(value, 3), "unit": "TFLOP/s",
-        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": round(total_ms / args.steps, 5), "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "f16",
-        "data": "synthetic (seeded N(0, 0.5^2))",
-        "config": {"workload": "causal prefill f16: 8 x 1024 tokens, 16 heads x 128, paged "
-                               "block 16", "flops_per_step": int(flops),
-                   "l2": "flushed between steps: 256 MB write then 256 MB read of a second "
-                         "buffer, outside the step events"},
-        "roofline": {"bound": "tensor", "achieved": round(achieved, 2), "peak": peak,
-                     "unit": "TFLOP/s", "frac": round(achieved / peak, 4),
-                     "peak_kind": f"{peak_kind} bf16_tflops (dense f16 = bf16 rate)",
-                     "traffic": read_traffic("paged_prefill_prefill_f16")},
-        "gpu_launches": args.steps, "clocks": clocks.summary(),
-    }
-    pool.close()
-    if rank == 0:
-        print(json.dumps(line), flush=True)
-    if dist is not None:
-        dist.destroy_process_group()
 
 
 def cpu_projection_baseline(batch, seconds: float):
@@ -731,37 +977,13 @@ def run_projection(args, dist, world, rank, device, peaks, peak_kind):
             batch.hidden, batch.weights = attn.to(torch.bfloat16), w_o
         line["cpu_baseline"] = cpu_projection_baseline(batch, min(args.cpu_seconds, 10.0))
     pool.close()
-    if rank == 0:
-        print(json.dumps(line), flush=True)
-    if dist is not None:
-        dist.destroy_process_group()
+    return line
+
 
 
 # ---------------------------------------------------------------------------
-# reference arm
+# other workloads
 # ---------------------------------------------------------------------------
-def _timed_steps(args, dist, device, stream, flush, parts):
-    """Runs `parts` (list of callables) per step after a GPU sleep, each part
-    bracketed by its own events; returns per-part total ms (this rank)."""
-    import torch
-
-    events = [[(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-               for _ in parts] for _ in range(args.steps)]
-    barrier(dist)
-    torch.cuda.synchronize(device)
-    torch.cuda._sleep(int(2e6 + 3e5 * args.steps))
-    for i in range(args.steps):
-        flush.fill_(float(i))
-        for (start, end), part in zip(events[i], parts):
-            start.record(stream)
-            part()
-            end.record(stream)
-    torch.cuda.synchronize(device)
-    barrier(dist)
-    return [sum(events[i][k][0].elapsed_time(events[i][k][1]) for i in range(args.steps))
-            for k in range(len(parts))]
-
-
 def run_mixed(args, dist, world, rank, device, peaks, peak_kind):
     """Continuous-batching step: one decode launch over the decode sequences
     and one prefill launch over the chunks, back to back on one stream."""
@@ -792,7 +1014,7 @@ def run_mixed(args, dist, world, rank, device, peaks, peak_kind):
         prefill()
     pool.synchronize()
     with ClockSampler(device) as clocks:
-        ms_d, ms_p = _timed_steps(args, dist, device, stream, flush, [decode, prefill])
+        ms_d, ms_p = timed_region(args, dist, device, stream, flush, [decode, prefill])
     pool.synchronize()
     step_ms = max_over_ranks(dist, (ms_d + ms_p) / args.steps)
     dbytes = batch.decode_bytes()
@@ -815,64 +1037,13 @@ def run_mixed(args, dist, world, rank, device, peaks, peak_kind):
         "gpu_launches": 3 * args.steps, "clocks": clocks.summary(),
     }
     pool.close()
-    if rank == 0:
-        print(json.dumps(line), flush=True)
-    if dist is not None:
-        dist.destroy_process_group()
+    return line
 
 
-def run_long_sequence(args, dist, world, rank, device, peaks, peak_kind):
-    """One 131072-token sequence split across the ranks: per step, decode
-    partials over the local blocks into one packed [m | l | o] block, one NCCL
-    all-gather of the blocks, rank-order log-sum-exp merge. Timed per rank with
-    events, max over ranks."""
-    import torch
 
-    from inferlab_b200 import distributed, workloads as wl
-
-    batch = wl.long_sequence_shard(device, rank, world)
-    pool = batch.pool
-    stream = torch.cuda.current_stream(device)
-    flush = L2Flush(device)
-    local = int(batch.contexts[0])
-    workspace = pool.make_workspace(1, 32, local)
-
-    def step():
-        # partials written as one packed [m | l | o] block, one NCCL all-gather,
-        # one rank-order merge kernel
-        return distributed.decode_split_sequence(pool, batch.queries, batch.block_tables, local,
-                                                 workspace=workspace)
-
-    for i in range(args.warmup):
-        flush.fill_(float(i))
-        step()
-    pool.synchronize()
-    with ClockSampler(device) as clocks:
-        (ms,) = _timed_steps(args, dist, device, stream, flush, [step])
-    pool.synchronize()
-    total_ms = max_over_ranks(dist, ms)
-    kv_bytes = 131072 * 8 * 128 * 2 * 2
-    value = kv_bytes * args.steps / (total_ms * 1e-3) / 1e9
-    line = {
-        "metric": "long-sequence decode KV-bytes GB/s", "value": round(value, 3), "unit": "GB/s",
-        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": round(total_ms / args.steps, 5), "higher_is_better": True,
-        "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded)",
-        "config": {"workload": "one 131072-token sequence, GQA 32/8 x 128 bf16, blocks split "
-                               "across GPUs, NCCL all-gather of (m, l, o) + rank-order merge",
-                   "tokens_this_rank": local},
-        "roofline": {"bound": "hbm", "achieved_per_gpu": round(value / world, 2),
-                     "peak": peaks["hbm_gbs"], "unit": "GB/s",
-                     "frac": round(value / world / peaks["hbm_gbs"], 4)},
-        "gpu_launches": 3 * args.steps, "clocks": clocks.summary(),
-    }
-    pool.close()
-    if rank == 0:
-        print(json.dumps(line), flush=True)
-    if dist is not None:
-        dist.destroy_process_group()
-
-
+# ---------------------------------------------------------------------------
+# reference arm
+# ---------------------------------------------------------------------------
 def run_reference(args):
     world, rank, _ = dist_env()
     if rank != 0:
@@ -890,7 +1061,7 @@ def run_reference(args):
         return run_reference_projection(args, world)
     if args.workload == "mixed_bf16":
         return run_reference_mixed(args, world)
-    if args.workload in ("longctx_bf16", "longseq_split"):
+    if args.workload in ("default", "longctx_bf16", "longseq_split"):
         return run_reference_long(args, world)
     if args.workload != "decode_fp32":
         print(json.dumps({"impl": "reference",
@@ -1117,11 +1288,19 @@ def run_reference_long(args, world):
               else "4 of the 256 sequences (contexts " + ", ".join(str(int(c)) for c in contexts)
               + ")")
     line = _reference_line(
-        args, world, "decode attn KV-bytes GB/s", value, "GB/s",
-        ("one 131,072-token sequence, GQA 32/8 x 128 bf16" if longseq
-         else "256 seqs x ctx U[4096, 32768], GQA 32/8 x 128 bf16"), threads,
+        args, world, "long-sequence decode KV-bytes GB/s" if longseq else "decode attn KV-bytes GB/s",
+        value, "GB/s",
+        ("one 131072-token sequence, GQA 32/8 x 128 bf16, blocks split across GPUs, NCCL "
+         "all-gather of (m, l, o) + rank-order merge" if longseq
+         else "paged decode bf16: 256 seqs x ctx U[4096,32768], GQA 32q/8kv x 128, block 16, "
+              "sequences sharded across GPUs"), threads,
         f"each step = {sample}: page gather + one inferlab_attention_forward call per q-head "
-        "(OnlineTiled, tile 16, Bf16 mode) from oracle/_ref/libref.so", "bf16")
+        "(OnlineTiled, tile 16, Bf16 mode) from oracle/_ref/libref.so, on the host cores of "
+        "one node whatever the GPU count", "bf16")
+    if not longseq:
+        line["config"].update({"num_seqs_total": 256, "q_heads": 32, "kv_heads": 8,
+                               "head_dim": 128, "block_tokens": 16, "seed": 2027})
+    line["scaling"] = "strong"
     line["ms_per_step"] = round(elapsed / args.steps * 1e3, 4)
     print(json.dumps(line), flush=True)
 
@@ -1179,11 +1358,14 @@ def main():
     parser.add_argument("--steps", type=int, default=20)
     parser.add_argument("--warmup", type=int, default=5)
     parser.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    parser.add_argument("--workload", default="decode_fp32",
-                        choices=["decode_fp32", "longctx_bf16", "prefill_f16", "mixed_bf16",
-                                 "longseq_split", "single_seq_fp32", "qkv_append_bf16",
-                                 "outproj_bf16"])
-    parser.add_argument("--cpu-seconds", type=float, default=10.0)
+    parser.add_argument("--workload", default="default",
+                        choices=["default", "longctx_bf16", "decode_fp32", "prefill_f16",
+                                 "mixed_bf16", "longseq_split", "single_seq_fp32",
+                                 "qkv_append_bf16", "outproj_bf16"])
+    parser.add_argument("--longctx-seqs", type=int, default=256,
+                        help="take the first N of the 256 long-context sequences (small "
+                             "profiling cases)")
+    parser.add_argument("--cpu-seconds", type=float, default=8.0)
     parser.add_argument("--no-cpu-baseline", action="store_true")
     args = parser.parse_args()
     args.warmup = max(args.warmup, 3)  # at least three untimed warm-up steps

@@ -13,6 +13,7 @@ ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 
 
 @pytest.mark.parametrize("workload,metric", [
+    ("default", "decode attn KV-bytes GB/s"),
     ("qkv_append_bf16", "qkv projection + paged append TFLOP/s"),
     ("outproj_bf16", "output projection + residual TFLOP/s"),
 ])
@@ -25,6 +26,7 @@ def test_reference_arm_line(workload, metric):
     assert line["impl"] == "reference"
     if "unavailable" in line:
         return
-    assert line["metric"] == metric and line["unit"] == "TFLOP/s" and line["value"] > 0
+    unit = "GB/s" if metric.endswith("GB/s") else "TFLOP/s"
+    assert line["metric"] == metric and line["unit"] == unit and line["value"] > 0
     assert line["cpu_baseline"]["kind"] == "reference" and line["cpu_baseline"]["cores"] >= 1
     assert line["e2e"]["h2d_bytes_per_step"] == 0 and line["e2e"]["value"] == line["value"]

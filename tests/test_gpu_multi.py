@@ -1,10 +1,11 @@
-"""Multi-GPU parity (needs >= 2 GPUs; skipped otherwise).
+"""Multi-GPU parity (needs 2, 4 or 8 GPUs; each case is skipped otherwise).
 
-One long sequence split across two GPUs by contiguous block ranges: each rank
-decodes its range into (m, l, o) partials, the partials are all-gathered over
-NCCL and merged in rank order; the result must equal the whole-context decode
-on one GPU within the fp32 tolerance |a - b| <= 1e-6 + 1e-5 |b|. Ranks are
-spawned processes with a short process-group timeout.
+One 131,072-token sequence (GQA 32/8 x 128, bf16) split across the GPUs by
+contiguous block ranges: each rank decodes its range into (m, l, o)
+partials, the partials are all-gathered over NCCL and merged in rank order;
+the result must equal the whole-context decode on one GPU within the fp32
+tolerance |a - b| <= 1e-6 + 1e-5 |b|. Ranks are spawned processes with a
+short process-group timeout.
 """
 import datetime
 import os
@@ -35,7 +36,7 @@ def _rank_main(rank, world, port, path):
                             timeout=datetime.timedelta(seconds=60),
                             device_id=torch.device(f"cuda:{rank}"))
     try:
-        total = 20000
+        total = 131072
         # every rank builds the same full sequence (same seed) so rank 0 can
         # also decode it whole; each rank then keeps only its own block range
         full = wl.decode_batch(rank, 77, 1, np.array([total]), 32, 8, 128, wl.KV_BF16,
@@ -53,15 +54,16 @@ def _rank_main(rank, world, port, path):
         dist.destroy_process_group()
 
 
-def test_split_sequence_over_nccl_matches_single_gpu(tmp_path):
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_split_sequence_over_nccl_matches_single_gpu(tmp_path, world):
     import torch
     import torch.multiprocessing as mp
 
-    if torch.cuda.device_count() < 2:
-        pytest.skip("needs two GPUs")
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
     path = str(tmp_path / "out.npy")
-    mp.start_processes(_rank_main, args=(2, _port(), path), nprocs=2, start_method="spawn",
-                       join=True)
+    mp.start_processes(_rank_main, args=(world, _port(), path), nprocs=world,
+                       start_method="spawn", join=True)
     merged, whole = np.load(path)
     err = np.abs(merged.astype(np.float64) - whole)
     assert np.all(err <= 1e-6 + 1e-5 * np.abs(whole)), float(err.max())
