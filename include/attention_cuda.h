@@ -46,7 +46,10 @@ struct AttentionStats {
 float round_attention_value(float value, AttentionPrecision precision);
 
 // Replaces kernels/attention_cpu.h:39-51. Host pointers; runs on the current
-// CUDA device; throws std::runtime_error with the reference's messages.
+// CUDA device; throws std::runtime_error with the reference's messages. Same
+// arithmetic and tolerances as inferlab_attention_forward (include/
+// inferlab_attention.h), including its tensor-core route for large causal
+// Fp16 / Bf16 calls with head_dimension 128.
 void attention_forward(const float* queries, const float* keys, const float* values,
                        std::size_t query_tokens, std::size_t key_value_tokens,
                        std::size_t heads, std::size_t head_dimension,

@@ -73,7 +73,13 @@ typedef struct InferlabAttentionStats {
  * Runs on the calling thread's current CUDA device. Both algorithms run the
  * same fused online-softmax kernel in fp32 (storage rounding applied on load);
  * the output matches either CPU algorithm within 1e-5 relative / 1e-6 absolute.
- * head_dimension is limited to 4096 on the device.
+ * Exception: causal calls in the Fp16 / Bf16 storage modes with head_dimension
+ * 128 and at least 1024 query rows (query_tokens x heads; the full-prompt call
+ * of Model::forward_all, worker/cpp/inferlab_runtime.cpp:1327-1339) run on the
+ * tensor cores with fp16 probabilities: within 2e-3 relative plus 1e-3 of the
+ * row's largest output. Inputs whose rounded values leave fp16's range (bf16
+ * V above 65504, fp16 overflow) fall back to the fp32 kernel. Stats are
+ * exact either way. head_dimension is limited to 4096 on the device.
  */
 int inferlab_attention_forward(const float* queries, const float* keys, const float* values,
                                size_t query_tokens, size_t key_value_tokens, size_t heads,

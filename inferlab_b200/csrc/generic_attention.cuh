@@ -45,6 +45,12 @@ struct ContiguousKv {
     __device__ __forceinline__ float load(const Row& row, std::uint32_t dim) const {
         return round_reference(row.ptr[dim], precision);
     }
+    // Four consecutive dimensions (dim a multiple of 4, head_dim too).
+    __device__ __forceinline__ float4 load4(const Row& row, std::uint32_t dim) const {
+        const float4 x = *reinterpret_cast<const float4*>(row.ptr + dim);
+        return make_float4(round_reference(x.x, precision), round_reference(x.y, precision),
+                           round_reference(x.z, precision), round_reference(x.w, precision));
+    }
 };
 
 // Key/value access through a block table into a pool arena
@@ -85,6 +91,17 @@ struct PagedKv {
     }
     __device__ __forceinline__ float load(const Row& row, std::uint32_t dim) const {
         return Storage<T>::to_float(row.ptr[dim]);
+    }
+    // Four consecutive dimensions (dim a multiple of 4, head_dim too).
+    __device__ __forceinline__ float4 load4(const Row& row, std::uint32_t dim) const {
+        if constexpr (sizeof(T) == 4) {
+            return *reinterpret_cast<const float4*>(row.ptr + dim);
+        } else {
+            const uint2 raw = *reinterpret_cast<const uint2*>(row.ptr + dim);
+            const T* h = reinterpret_cast<const T*>(&raw);
+            return make_float4(Storage<T>::to_float(h[0]), Storage<T>::to_float(h[1]),
+                               Storage<T>::to_float(h[2]), Storage<T>::to_float(h[3]));
+        }
     }
 };
 
@@ -174,14 +191,22 @@ __global__ void __launch_bounds__(kGenericWarps * 32)
 
     // Finite check of the raw inputs, spread over the whole grid
     // (kernels/attention_cpu.cpp:131-134 checks every element).
+    // Four loads in flight per thread; the entry sizes the grid so that a
+    // call with few query rows still spreads the check over enough CTAs.
     for (int t = 0; t < 3; ++t) {
         const float* ptr = p.check_ptr[t];
         if (ptr == nullptr) continue;
         bool bad = false;
-        for (std::size_t i = static_cast<std::size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-             i < p.check_count[t]; i += static_cast<std::size_t>(gridDim.x) * blockDim.x) {
-            bad |= !isfinite(ptr[i]);
+        const std::size_t stride = static_cast<std::size_t>(gridDim.x) * blockDim.x;
+        std::size_t i = static_cast<std::size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+        for (; i + 3 * stride < p.check_count[t]; i += 4 * stride) {
+            const float a = ptr[i];
+            const float b = ptr[i + stride];
+            const float c = ptr[i + 2 * stride];
+            const float e = ptr[i + 3 * stride];
+            bad |= !(isfinite(a) && isfinite(b) && isfinite(c) && isfinite(e));
         }
+        for (; i < p.check_count[t]; i += stride) bad |= !isfinite(ptr[i]);
         if (bad) flag_error(p.error_word, kErrNonFinite);
     }
 
@@ -212,23 +237,55 @@ __global__ void __launch_bounds__(kGenericWarps * 32)
     for (long long begin = 0; begin < legal; begin += kGenericChunk) {
         float score[kGenericTpl];
         float chunk_max = -INFINITY;
+        // Scores of this lane's kTpl keys. The dot products keep the
+        // reference's order and rounding (kernels/attention_cpu.cpp:245-251):
+        // sequential over the head dimension, product and sum rounded
+        // separately, so the scores - whose errors exp() amplifies - agree
+        // exactly. The loads of all kTpl keys are issued together (four
+        // dimensions at a time when head_dim allows), so a key costs one
+        // memory round trip per four dimensions, not one per dimension.
+        typename Kv::Row krow[kGenericTpl];
+        bool valid[kGenericTpl];
 #pragma unroll
         for (int j = 0; j < kGenericTpl; ++j) {
             const long long token = begin + j * 32 + lane;
-            score[j] = -INFINITY;
-            if (token < legal) {
-                const auto krow = kv.key_row(segment, token, kv_head);
-                float s = 0.0f;
-                // Same order and rounding as the reference's dot product
-                // (kernels/attention_cpu.cpp:245-251): sequential over the
-                // head dimension, product and sum rounded separately, so the
-                // scores - whose errors exp() amplifies - agree exactly.
-                for (unsigned c = 0; c < d; ++c) {
-                    s = __fadd_rn(s, __fmul_rn(q_s[c], kv.load(krow, c)));
+            valid[j] = token < legal;
+            krow[j] = kv.key_row(segment, valid[j] ? token : begin, kv_head);
+            score[j] = 0.0f;
+        }
+        if ((d & 3u) == 0) {
+#pragma unroll 2
+            for (unsigned c = 0; c < d; c += 4) {
+                float4 k4[kGenericTpl];
+#pragma unroll
+                for (int j = 0; j < kGenericTpl; ++j) {
+                    k4[j] = valid[j] ? kv.load4(krow[j], c) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
                 }
-                score[j] = __fmul_rn(s, p.scale);
-                chunk_max = fmaxf(chunk_max, score[j]);
+#pragma unroll
+                for (int j = 0; j < kGenericTpl; ++j) {
+                    float s_ = score[j];
+                    s_ = __fadd_rn(s_, __fmul_rn(q_s[c], k4[j].x));
+                    s_ = __fadd_rn(s_, __fmul_rn(q_s[c + 1], k4[j].y));
+                    s_ = __fadd_rn(s_, __fmul_rn(q_s[c + 2], k4[j].z));
+                    s_ = __fadd_rn(s_, __fmul_rn(q_s[c + 3], k4[j].w));
+                    score[j] = s_;
+                }
             }
+        } else {
+            for (unsigned c = 0; c < d; ++c) {
+                float k1[kGenericTpl];
+#pragma unroll
+                for (int j = 0; j < kGenericTpl; ++j) k1[j] = valid[j] ? kv.load(krow[j], c) : 0.0f;
+#pragma unroll
+                for (int j = 0; j < kGenericTpl; ++j) {
+                    score[j] = __fadd_rn(score[j], __fmul_rn(q_s[c], k1[j]));
+                }
+            }
+        }
+#pragma unroll
+        for (int j = 0; j < kGenericTpl; ++j) {
+            score[j] = valid[j] ? __fmul_rn(score[j], p.scale) : -INFINITY;
+            chunk_max = fmaxf(chunk_max, score[j]);
         }
         chunk_max = warp_max(chunk_max);
         const float new_max = fmaxf(running_max, chunk_max);
@@ -246,7 +303,18 @@ __global__ void __launch_bounds__(kGenericWarps * 32)
         const long long count = min(static_cast<long long>(kGenericChunk), legal - begin);
         for (unsigned c = lane; c < d; c += 32) {
             float a = acc_s[c] * alpha;
-            for (long long t = 0; t < count; ++t) {
+            long long t = 0;
+            // Eight value loads in flight, accumulated in token order.
+            for (; t + 8 <= count; t += 8) {
+                float v8[8];
+#pragma unroll
+                for (int u = 0; u < 8; ++u) {
+                    v8[u] = kv.load(kv.value_row(segment, begin + t + u, kv_head), c);
+                }
+#pragma unroll
+                for (int u = 0; u < 8; ++u) a = fmaf(p_s[t + u], v8[u], a);
+            }
+            for (; t < count; ++t) {
                 const auto vrow = kv.value_row(segment, begin + t, kv_head);
                 a = fmaf(p_s[t], kv.load(vrow, c), a);
             }

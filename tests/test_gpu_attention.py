@@ -192,3 +192,44 @@ int main() {
     close(got, ref)
     assert int(lines[48]) == stats["score_elements"]
     assert " ".join(lines[49:]) == "causal query positions exceed the KV sequence"
+
+
+@pytest.mark.parametrize("precision", [1, 2])
+@pytest.mark.parametrize("algorithm", [0, 1])
+@pytest.mark.parametrize("tq,tkv,h,start", [(512, 512, 8, 0), (300, 700, 4, 400),
+                                            (1024, 1030, 2, 6)])
+def test_tensor_route_fp16_bf16_modes(il, oracle_mod, precision, algorithm, tq, tkv, h, start):
+    """Fp16 / Bf16 storage mode, head_dim 128, causal, at least 1024 query rows:
+    the drop-in entry runs the tensor-core prefill. Against the reference's
+    own mode (the oracle rounds inputs as round_attention_value does, then
+    computes in fp32) the tolerance is the f16/bf16 one, |gpu - ref| <=
+    2e-3 |ref| + 1e-3 max|ref row| (fp16 probabilities); stats are exact."""
+    rng = np.random.Generator(np.random.PCG64(tq + 10 * h + precision))
+    q = rng.standard_normal(tq * h * 128, dtype=np.float32)
+    k = rng.standard_normal(tkv * h * 128, dtype=np.float32)
+    v = rng.standard_normal(tkv * h * 128, dtype=np.float32)
+    got = run(il, q, k, v, tq, tkv, h, 128, start, algorithm, precision)
+    ref, ref_stats = oracle_mod.attention_forward(q, k, v, tq, tkv, h, 128, start, algorithm,
+                                                  precision, 16)
+    got_rows = np.asarray(got.output, np.float64).reshape(-1, 128)
+    ref_rows = np.asarray(ref, np.float64).reshape(-1, 128)
+    err = np.abs(got_rows - ref_rows)
+    bound = 2e-3 * np.abs(ref_rows) + 1e-3 * np.max(np.abs(ref_rows), axis=1, keepdims=True)
+    assert np.all(err <= bound), f"max abs err {err.max():.3e}"
+    assert got.stats.as_dict() == ref_stats
+
+
+def test_tensor_route_falls_back_for_values_beyond_fp16(il, oracle_mod):
+    """A Bf16-mode V value beyond fp16's range (the tensor path widens V to
+    fp16) sends the call back to the fp32 kernel: the result then meets the
+    fp32 tolerance against the oracle."""
+    rng = np.random.Generator(np.random.PCG64(77))
+    tq, h = 512, 4
+    q = rng.standard_normal(tq * h * 128, dtype=np.float32)
+    k = rng.standard_normal(tq * h * 128, dtype=np.float32)
+    v = rng.standard_normal(tq * h * 128, dtype=np.float32)
+    v[12345] = 1.0e5
+    got = run(il, q, k, v, tq, tq, h, 128, 0, 1, 2)
+    ref, ref_stats = oracle_mod.attention_forward(q, k, v, tq, tq, h, 128, 0, 1, 2, 16)
+    close(got.output, ref)
+    assert got.stats.as_dict() == ref_stats
