@@ -15,9 +15,12 @@ context lengths; value = all ranks' bytes / the slowest rank's time. Beside it,
 each timed in the same run, are the other halves of the metric:
 prefill_f16 (causal prefill 8 x 1024 tokens, 16 heads x 128, f16; TFLOP/s per
 rank, one batch per rank), decode_fp32 (64 sequences x U[64, 2048], 8 heads x
-64, fp32; one batch per rank) and longseq_split (one 131,072-token sequence
+64, fp32; one batch per rank), longseq_split (one 131,072-token sequence
 split across the ranks by contiguous block ranges, partials all-gathered over
-NCCL and merged in rank order). Every object carries its roofline, per-rank
+NCCL and merged in rank order), mixed_bf16 (one continuous-batching step per
+rank: its decode launch and its chunked-prefill launch) and single_seq_fp32
+(the drop-in C entry on the reference's own 129 x 4 x 32 case, microseconds
+per prefill + decode call pair). Every object carries its roofline, per-rank
 step times and clocks; at N = 1 the CPU baseline legs time the reference's
 own kernel (oracle/_ref/libref.so, built from kernels/attention_cpu.cpp) on a
 bounded sample of the same data and record how its outputs compare with ours.
@@ -752,6 +755,8 @@ def run_default(args, dist, world, rank, device, peaks, peak_kind):
                                          "decode_fp32")
     line["longseq_split"] = measure_long_sequence(args, dist, world, rank, device, peaks,
                                                   peak_kind)
+    line["mixed_bf16"] = run_mixed(args, dist, world, rank, device, peaks, peak_kind)
+    line["single_seq_fp32"] = run_single_sequence(args, dist, world, rank, device)
     return line
 
 
@@ -838,7 +843,7 @@ def run_single_sequence(args, dist, world, rank, device):
                    "timing": "host clock, median of steps; launch-bound, no roofline claim"},
         "gpu_launches": 2 * args.steps,
     }
-    if rank == 0 and not args.no_cpu_baseline and oracle.ref_lib() is not None:
+    if rank == 0 and world == 1 and not args.no_cpu_baseline and oracle.ref_lib() is not None:
         for _ in range(3):
             reference()
         ref_times = []
@@ -1034,7 +1039,9 @@ def run_mixed(args, dist, world, rank, device, peaks, peak_kind):
         "prefill": {"ms": round(ms_p / args.steps, 5),
                     "TFLOP/s": round(flops / (ms_p / args.steps) / 1e9, 2),
                     "frac_tensor": round(flops / (ms_p / args.steps) / 1e9 / peaks["bf16_tflops"], 4)},
-        "gpu_launches": 3 * args.steps, "clocks": clocks.summary(),
+        "gpu_launches": 2 * args.steps, "clocks": clocks.summary(),
+        "per_rank": per_rank(dist, ms_per_step=(ms_d + ms_p) / args.steps,
+                             decode_ms=ms_d / args.steps, prefill_ms=ms_p / args.steps),
     }
     pool.close()
     return line
