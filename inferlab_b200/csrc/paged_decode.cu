@@ -98,14 +98,52 @@ struct DecodeSmem {
         static_cast<std::size_t>(kDecodeWarps) * kDecodeStages * 2 * S::kTileBytes;
     static constexpr std::size_t kBars = kTilesBytes;
     static constexpr std::size_t kIds = kBars + kDecodeWarps * kDecodeStages * 8;
-    static constexpr std::size_t kRedAcc = kIds + kMaxBlocksPerSplit * 4;
-    static constexpr std::size_t kRedMl = kRedAcc + static_cast<std::size_t>(kDecodeWarps) * GROUP * D * 4;
-    static constexpr std::size_t kFlag = kRedMl + kDecodeWarps * GROUP * 2 * 4;
+    static constexpr std::size_t kFlag = kIds + kMaxBlocksPerSplit * 4;
     static constexpr std::size_t kBytes = kFlag + 16;
+    // Each warp's end-of-stream state (acc per q-head of the group, then
+    // (m, l) per q-head) goes into the start of its own tile ring, which its
+    // copies no longer use by then: no separate reduction area, so the
+    // 16-bit GQA kernels fit three CTAs per SM.
+    static constexpr std::size_t kWarpRegion = static_cast<std::size_t>(kDecodeStages) * 2 * S::kTileBytes;
+    static constexpr std::size_t kRedMlOff = static_cast<std::size_t>(GROUP) * D * 4;
+    static_assert(kRedMlOff + GROUP * 8 <= kWarpRegion, "warp state must fit its tile ring");
     static_assert(GROUP * kMaxSplits * 4 <= kTilesBytes, "split weights must fit the tile area");
 };
 
 __device__ __forceinline__ float safe_max(float m) { return m == -INFINITY ? 0.0f : m; }
+
+// Packed fp32 pairs (one f32x2 instruction for two lanes of work, each lane
+// rounded as a scalar fma.rn / mul.rn would be; no flush to zero).
+__device__ __forceinline__ std::uint64_t fma2(std::uint64_t a, std::uint64_t b, std::uint64_t c) {
+    std::uint64_t d;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+    return d;
+}
+__device__ __forceinline__ std::uint64_t mul2(std::uint64_t a, std::uint64_t b) {
+    std::uint64_t d;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+
+// A 16-byte chunk of storage elements as fp32 pairs (element 2i low, 2i + 1 high).
+__device__ __forceinline__ void widen16_pairs(const uint4& raw, std::uint64_t* out, float) {
+    out[0] = pack_u32x2(raw.x, raw.y);
+    out[1] = pack_u32x2(raw.z, raw.w);
+}
+__device__ __forceinline__ void widen16_pairs(const uint4& raw, std::uint64_t* out, __half) {
+    const __half2* h = reinterpret_cast<const __half2*>(&raw);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const float2 f = __half22float2(h[i]);
+        out[i] = pack_f32x2(f.x, f.y);
+    }
+}
+__device__ __forceinline__ void widen16_pairs(const uint4& raw, std::uint64_t* out, __nv_bfloat16) {
+    // bf16 -> fp32 is a 16-bit shift of the bit pattern.
+    const std::uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) out[i] = pack_u32x2(w[i] << 16, w[i] & 0xFFFF0000u);
+}
 
 template <typename KvT, int D, int GROUP>
 __global__ void __launch_bounds__(kDecodeWarps * 32)
@@ -115,8 +153,12 @@ __global__ void __launch_bounds__(kDecodeWarps * 32)
     extern __shared__ __align__(128) unsigned char smem[];
     auto* bars = reinterpret_cast<std::uint64_t*>(smem + L::kBars);
     auto* ids = reinterpret_cast<std::int32_t*>(smem + L::kIds);
-    auto* red_acc = reinterpret_cast<float*>(smem + L::kRedAcc);
-    auto* red_ml = reinterpret_cast<float*>(smem + L::kRedMl);
+    auto red_acc = [&](int w, int h) {
+        return reinterpret_cast<float*>(smem + w * L::kWarpRegion + static_cast<std::size_t>(h) * D * 4);
+    };
+    auto red_ml = [&](int w, int h) {
+        return reinterpret_cast<float*>(smem + w * L::kWarpRegion + L::kRedMlOff + h * 8);
+    };
     auto* flag = reinterpret_cast<int*>(smem + L::kFlag);
 
     const int warp = threadIdx.x >> 5;
@@ -172,7 +214,10 @@ __global__ void __launch_bounds__(kDecodeWarps * 32)
     // Q in its Fp16/Bf16 modes, kernels/attention_cpu.cpp:456-457).
     const int ts = lane / S::kG;
     const int cg = lane % S::kG;
-    float q[GROUP][S::kDpl];
+    // q and the accumulators are held as fp32 pairs (dims 2i, 2i + 1), so the
+    // dot products and the P x V update take one f32x2 FMA per two dims: the
+    // kernel is bound by instruction issue, not by the fp32 pipe.
+    std::uint64_t q2[GROUP][S::kDpl / 2];
     bool q_bad = false;
 #pragma unroll
     for (int h = 0; h < GROUP; ++h) {
@@ -183,12 +228,12 @@ __global__ void __launch_bounds__(kDecodeWarps * 32)
 #pragma unroll
             for (int e = 0; e < S::kEpc; e += 4) {
                 const float4 v = *reinterpret_cast<const float4*>(qrow + base + e);
-                const float raw[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-                for (int t = 0; t < 4; ++t) {
-                    q_bad |= !isfinite(raw[t]);
-                    q[h][c * S::kEpc + e + t] = round_storage(raw[t], Storage<KvT>::kType);
-                }
+                q_bad |= !(isfinite(v.x) && isfinite(v.y) && isfinite(v.z) && isfinite(v.w));
+                const int i = (c * S::kEpc + e) / 2;
+                q2[h][i] = pack_f32x2(round_storage(v.x, Storage<KvT>::kType),
+                                      round_storage(v.y, Storage<KvT>::kType));
+                q2[h][i + 1] = pack_f32x2(round_storage(v.z, Storage<KvT>::kType),
+                                          round_storage(v.w, Storage<KvT>::kType));
             }
         }
     }
@@ -215,13 +260,13 @@ __global__ void __launch_bounds__(kDecodeWarps * 32)
 
     float m[GROUP];
     float l[GROUP];
-    float acc[GROUP][S::kDpl];
+    std::uint64_t acc2[GROUP][S::kDpl / 2];
 #pragma unroll
     for (int h = 0; h < GROUP; ++h) {
         m[h] = -INFINITY;
         l[h] = 0.0f;
 #pragma unroll
-        for (int e = 0; e < S::kDpl; ++e) acc[h][e] = 0.0f;
+        for (int e = 0; e < S::kDpl / 2; ++e) acc2[h][e] = 0;
     }
 
     int consumed = 0;
@@ -243,23 +288,25 @@ __global__ void __launch_bounds__(kDecodeWarps * 32)
 #pragma unroll
         for (int r = 0; r < S::kR; ++r) {
             const int trow = ts + S::kTS * r;
-            float part[GROUP];
+            std::uint64_t part2[GROUP];
 #pragma unroll
-            for (int h = 0; h < GROUP; ++h) part[h] = 0.0f;
+            for (int h = 0; h < GROUP; ++h) part2[h] = 0;
 #pragma unroll
             for (int c = 0; c < S::kCh; ++c) {
                 const uint4 raw = *reinterpret_cast<const uint4*>(
                     ktile + (static_cast<std::size_t>(trow) * S::kChunks + cg + S::kG * c) * 16);
-                float kf[S::kEpc];
-                widen16(raw, kf, KvT{});
+                std::uint64_t k2[S::kEpc / 2];
+                widen16_pairs(raw, k2, KvT{});
 #pragma unroll
                 for (int h = 0; h < GROUP; ++h) {
 #pragma unroll
-                    for (int e = 0; e < S::kEpc; ++e) part[h] = fmaf(q[h][c * S::kEpc + e], kf[e], part[h]);
+                    for (int e = 0; e < S::kEpc / 2; ++e) {
+                        part2[h] = fma2(q2[h][c * S::kEpc / 2 + e], k2[e], part2[h]);
+                    }
                 }
             }
 #pragma unroll
-            for (int h = 0; h < GROUP; ++h) s[h][r] = part[h];
+            for (int h = 0; h < GROUP; ++h) s[h][r] = low_f32(part2[h]) + high_f32(part2[h]);
         }
 #pragma unroll
         for (int off = 1; off < S::kG; off <<= 1) {
@@ -288,8 +335,9 @@ __global__ void __launch_bounds__(kDecodeWarps * 32)
                 sum += s[h][r];
             }
             l[h] = l[h] * alpha + sum;
+            const std::uint64_t alpha2 = pack_f32x2(alpha, alpha);
 #pragma unroll
-            for (int e = 0; e < S::kDpl; ++e) acc[h][e] *= alpha;
+            for (int e = 0; e < S::kDpl / 2; ++e) acc2[h][e] = mul2(acc2[h][e], alpha2);
         }
 #pragma unroll
         for (int r = 0; r < S::kR; ++r) {
@@ -299,13 +347,14 @@ __global__ void __launch_bounds__(kDecodeWarps * 32)
             for (int c = 0; c < S::kCh; ++c) {
                 const uint4 raw = *reinterpret_cast<const uint4*>(
                     vtile + (static_cast<std::size_t>(trow) * S::kChunks + cg + S::kG * c) * 16);
-                float vf[S::kEpc];
-                widen16(raw, vf, KvT{});
+                std::uint64_t v2[S::kEpc / 2];
+                widen16_pairs(raw, v2, KvT{});
 #pragma unroll
                 for (int h = 0; h < GROUP; ++h) {
+                    const std::uint64_t s2 = pack_f32x2(s[h][r], s[h][r]);
 #pragma unroll
-                    for (int e = 0; e < S::kEpc; ++e) {
-                        acc[h][c * S::kEpc + e] = fmaf(s[h][r], vf[e], acc[h][c * S::kEpc + e]);
+                    for (int e = 0; e < S::kEpc / 2; ++e) {
+                        acc2[h][c * S::kEpc / 2 + e] = fma2(s2, v2[e], acc2[h][c * S::kEpc / 2 + e]);
                     }
                 }
             }
@@ -334,9 +383,12 @@ __global__ void __launch_bounds__(kDecodeWarps * 32)
             const float b = exp2f(mo - base);
             l[h] = l[h] * a + lo * b;
 #pragma unroll
-            for (int e = 0; e < S::kDpl; ++e) {
-                const float other = __shfl_xor_sync(0xffffffffu, acc[h][e], off);
-                acc[h][e] = acc[h][e] * a + other * b;
+            for (int e = 0; e < S::kDpl / 2; ++e) {
+                const float x0 = low_f32(acc2[h][e]);
+                const float x1 = high_f32(acc2[h][e]);
+                const float o0 = __shfl_xor_sync(0xffffffffu, x0, off);
+                const float o1 = __shfl_xor_sync(0xffffffffu, x1, off);
+                acc2[h][e] = pack_f32x2(x0 * a + o0 * b, x1 * a + o1 * b);
             }
             m[h] = mn;
         }
@@ -344,17 +396,19 @@ __global__ void __launch_bounds__(kDecodeWarps * 32)
     if (ts == 0) {
 #pragma unroll
         for (int h = 0; h < GROUP; ++h) {
-            float* dst = red_acc + (static_cast<std::size_t>(warp) * GROUP + h) * D;
+            float* dst = red_acc(warp, h);
 #pragma unroll
             for (int c = 0; c < S::kCh; ++c) {
 #pragma unroll
-                for (int e = 0; e < S::kEpc; ++e) {
-                    dst[(cg + S::kG * c) * S::kEpc + e] = acc[h][c * S::kEpc + e];
+                for (int e = 0; e < S::kEpc / 2; ++e) {
+                    const std::uint64_t x = acc2[h][c * S::kEpc / 2 + e];
+                    dst[(cg + S::kG * c) * S::kEpc + 2 * e] = low_f32(x);
+                    dst[(cg + S::kG * c) * S::kEpc + 2 * e + 1] = high_f32(x);
                 }
             }
             if (cg == 0) {
-                red_ml[(warp * GROUP + h) * 2] = m[h];
-                red_ml[(warp * GROUP + h) * 2 + 1] = l[h];
+                red_ml(warp, h)[0] = m[h];
+                red_ml(warp, h)[1] = l[h];
             }
         }
     }
@@ -368,15 +422,15 @@ __global__ void __launch_bounds__(kDecodeWarps * 32)
         const int dim = i % D;
         float mw = -INFINITY;
 #pragma unroll
-        for (int w = 0; w < kDecodeWarps; ++w) mw = fmaxf(mw, red_ml[(w * GROUP + h) * 2]);
+        for (int w = 0; w < kDecodeWarps; ++w) mw = fmaxf(mw, red_ml(w, h)[0]);
         const float base = safe_max(mw);
         float lsum = 0.0f;
         float a = 0.0f;
 #pragma unroll
         for (int w = 0; w < kDecodeWarps; ++w) {
-            const float f = exp2f(red_ml[(w * GROUP + h) * 2] - base);
-            lsum += red_ml[(w * GROUP + h) * 2 + 1] * f;
-            a += red_acc[(static_cast<std::size_t>(w) * GROUP + h) * D + dim] * f;
+            const float f = exp2f(red_ml(w, h)[0] - base);
+            lsum += red_ml(w, h)[1] * f;
+            a += red_acc(w, h)[dim] * f;
         }
         const std::size_t row = row0 + h;
         if (single) {
@@ -413,7 +467,7 @@ __global__ void __launch_bounds__(kDecodeWarps * 32)
     __threadfence();
     // Split weights, once per q-head (one warp per head), into the tile area,
     // which no copy uses any more: w[h][sp] = 2^(m_sp - M_h), and per head
-    // (M_h, L_h = sum_sp l_sp w[h][sp]) into red_ml.
+    // (M_h, L_h = sum_sp l_sp w[h][sp]) into warp 0's (m, l) slots.
     float* w = reinterpret_cast<float*>(smem);
     for (int h = warp; h < GROUP; h += kDecodeWarps) {
         const float* ml = p.ws_ml + (row0 + h) * p.max_splits * 2;
@@ -429,8 +483,8 @@ __global__ void __launch_bounds__(kDecodeWarps * 32)
         }
         lsum = warp_sum(lsum);
         if (lane == 0) {
-            red_ml[h * 2] = mw;
-            red_ml[h * 2 + 1] = lsum;
+            red_ml(0, h)[0] = mw;
+            red_ml(0, h)[1] = lsum;
         }
     }
     __syncthreads();
@@ -465,8 +519,8 @@ __global__ void __launch_bounds__(kDecodeWarps * 32)
             a.z = fmaf(x.z, f, a.z);
             a.w = fmaf(x.w, f, a.w);
         }
-        const float mw = red_ml[h * 2];
-        const float lsum = red_ml[h * 2 + 1];
+        const float mw = red_ml(0, h)[0];
+        const float lsum = red_ml(0, h)[1];
         if (p.emit_partials) {
             *reinterpret_cast<float4*>(p.part_o + row * D + dim) = a;
             if (dim == 0) {
