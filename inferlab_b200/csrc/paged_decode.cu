@@ -34,6 +34,8 @@
 
 #include <algorithm>
 #include <cmath>
+#include <map>
+#include <mutex>
 
 namespace ilb {
 namespace {
@@ -45,6 +47,8 @@ constexpr int kMaxBlocksPerSplit = 1024;
 // Splits per context are capped so that the last CTA's merge stays short
 // (at 64 splits it reads 64 x (head_dim + 2) floats per q-head).
 constexpr std::uint32_t kMaxSplits = 64;
+
+constexpr int ilog2(int x) { return x <= 1 ? 0 : 1 + ilog2(x / 2); }
 
 template <typename KvT, int D, int GROUP>
 struct DecodeShape {
@@ -59,6 +63,9 @@ struct DecodeShape {
     static constexpr int kR = kDecodeBlockTokens / kTS;  // tokens per slot per block
     static constexpr int kDpl = kCh * kEpc;              // dims per lane
     static constexpr int kTileBytes = kDecodeBlockTokens * D * kElem;
+    // A token row's kG lanes split the heads of the group (kG / GROUP lanes
+    // per head) for the softmax instead of all running every head.
+    static constexpr bool kSplitHeads = GROUP >= 2 && kG >= GROUP && kG % GROUP == 0;
     static_assert(kChunks * 16 == D * kElem, "head_dim must fill 16-byte chunks");
     static_assert(kG >= 1 && kG <= 32 && 32 % kG == 0, "lane split");
     static_assert(kDecodeBlockTokens % kTS == 0, "token slots");
@@ -146,7 +153,9 @@ __device__ __forceinline__ void widen16_pairs(const uint4& raw, std::uint64_t* o
 }
 
 template <typename KvT, int D, int GROUP>
-__global__ void __launch_bounds__(kDecodeWarps * 32)
+// Three CTAs per SM for groups of up to four q-heads (the fp32 pairs of q and
+// the accumulators fit ~168 registers); GQA-8 keeps the compiler's choice.
+__global__ void __launch_bounds__(kDecodeWarps * 32, GROUP >= 8 ? 1 : 3)
     paged_decode_kernel(const DecodeParams p) {
     using S = DecodeShape<KvT, D, GROUP>;
     using L = DecodeSmem<KvT, D, GROUP>;
@@ -260,6 +269,9 @@ __global__ void __launch_bounds__(kDecodeWarps * 32)
 
     float m[GROUP];
     float l[GROUP];
+    float m_own = -INFINITY;  // head-split softmax: this lane's own head
+    float l_own = 0.0f;
+    const int slot_base = lane - cg;  // first lane of this token row
     std::uint64_t acc2[GROUP][S::kDpl / 2];
 #pragma unroll
     for (int h = 0; h < GROUP; ++h) {
@@ -308,36 +320,99 @@ __global__ void __launch_bounds__(kDecodeWarps * 32)
 #pragma unroll
             for (int h = 0; h < GROUP; ++h) s[h][r] = low_f32(part2[h]) + high_f32(part2[h]);
         }
+        if constexpr (S::kSplitHeads) {
+            // Reduce-scatter over the heads: each round halves the heads a
+            // lane holds, keeping the half with its own head (cg / kLph), then
+            // the kLph lanes of that head sum its scores. s[0] then holds this
+            // lane's own head.
+            constexpr int kLph = S::kG / GROUP;
 #pragma unroll
-        for (int off = 1; off < S::kG; off <<= 1) {
+            for (int k = 0; k < ilog2(GROUP); ++k) {
+                const int n = GROUP >> k;
+                const int off = S::kG >> (k + 1);
+                const bool upper = (cg & off) != 0;
 #pragma unroll
-            for (int h = 0; h < GROUP; ++h) {
+                for (int i = 0; i < n / 2; ++i) {
 #pragma unroll
-                for (int r = 0; r < S::kR; ++r) s[h][r] += __shfl_xor_sync(0xffffffffu, s[h][r], off);
+                    for (int r = 0; r < S::kR; ++r) {
+                        const float lo_v = s[i][r];
+                        const float hi_v = s[i + n / 2][r];
+                        const float keep = upper ? hi_v : lo_v;
+                        s[i][r] = keep + __shfl_xor_sync(0xffffffffu, upper ? lo_v : hi_v, off);
+                    }
+                }
             }
-        }
 #pragma unroll
-        for (int h = 0; h < GROUP; ++h) {
+            for (int off = kLph / 2; off >= 1; off >>= 1) {
+#pragma unroll
+                for (int r = 0; r < S::kR; ++r) s[0][r] += __shfl_xor_sync(0xffffffffu, s[0][r], off);
+            }
             float mx = -INFINITY;
 #pragma unroll
             for (int r = 0; r < S::kR; ++r) {
-                s[h][r] = (ts + S::kTS * r) < valid ? s[h][r] * p.scale_log2 : -INFINITY;
-                mx = fmaxf(mx, s[h][r]);
+                s[0][r] = (ts + S::kTS * r) < valid ? s[0][r] * p.scale_log2 : -INFINITY;
+                mx = fmaxf(mx, s[0][r]);
             }
-            const float m_new = fmaxf(m[h], mx);
+            const float m_new = fmaxf(m_own, mx);
             const float base = safe_max(m_new);
-            const float alpha = exp2f(m[h] - base);
-            m[h] = m_new;
+            const float alpha_own = exp2f(m_own - base);
+            m_own = m_new;
             float sum = 0.0f;
 #pragma unroll
             for (int r = 0; r < S::kR; ++r) {
-                s[h][r] = exp2f(s[h][r] - base);
-                sum += s[h][r];
+                s[0][r] = exp2f(s[0][r] - base);
+                sum += s[0][r];
             }
-            l[h] = l[h] * alpha + sum;
-            const std::uint64_t alpha2 = pack_f32x2(alpha, alpha);
+            l_own = l_own * alpha_own + sum;
+            // Every head's probabilities and rescale factor from its lanes.
+            float p_all[GROUP][S::kR];
 #pragma unroll
-            for (int e = 0; e < S::kDpl / 2; ++e) acc2[h][e] = mul2(acc2[h][e], alpha2);
+            for (int h = 0; h < GROUP; ++h) {
+                const int src = slot_base + h * kLph;
+                const float alpha = __shfl_sync(0xffffffffu, alpha_own, src);
+#pragma unroll
+                for (int r = 0; r < S::kR; ++r) p_all[h][r] = __shfl_sync(0xffffffffu, s[0][r], src);
+                const std::uint64_t alpha2 = pack_f32x2(alpha, alpha);
+#pragma unroll
+                for (int e = 0; e < S::kDpl / 2; ++e) acc2[h][e] = mul2(acc2[h][e], alpha2);
+            }
+#pragma unroll
+            for (int h = 0; h < GROUP; ++h) {
+#pragma unroll
+                for (int r = 0; r < S::kR; ++r) s[h][r] = p_all[h][r];
+            }
+        } else {
+    #pragma unroll
+            for (int off = 1; off < S::kG; off <<= 1) {
+    #pragma unroll
+                for (int h = 0; h < GROUP; ++h) {
+    #pragma unroll
+                    for (int r = 0; r < S::kR; ++r) s[h][r] += __shfl_xor_sync(0xffffffffu, s[h][r], off);
+                }
+            }
+    #pragma unroll
+            for (int h = 0; h < GROUP; ++h) {
+                float mx = -INFINITY;
+    #pragma unroll
+                for (int r = 0; r < S::kR; ++r) {
+                    s[h][r] = (ts + S::kTS * r) < valid ? s[h][r] * p.scale_log2 : -INFINITY;
+                    mx = fmaxf(mx, s[h][r]);
+                }
+                const float m_new = fmaxf(m[h], mx);
+                const float base = safe_max(m_new);
+                const float alpha = exp2f(m[h] - base);
+                m[h] = m_new;
+                float sum = 0.0f;
+    #pragma unroll
+                for (int r = 0; r < S::kR; ++r) {
+                    s[h][r] = exp2f(s[h][r] - base);
+                    sum += s[h][r];
+                }
+                l[h] = l[h] * alpha + sum;
+                const std::uint64_t alpha2 = pack_f32x2(alpha, alpha);
+    #pragma unroll
+                for (int e = 0; e < S::kDpl / 2; ++e) acc2[h][e] = mul2(acc2[h][e], alpha2);
+            }
         }
 #pragma unroll
         for (int r = 0; r < S::kR; ++r) {
@@ -361,6 +436,14 @@ __global__ void __launch_bounds__(kDecodeWarps * 32)
         }
         __syncwarp();
         if (lane == 0 && j + kDecodeStages < my_count) issue(j + kDecodeStages);
+    }
+    if constexpr (S::kSplitHeads) {
+#pragma unroll
+        for (int h = 0; h < GROUP; ++h) {
+            const int src = slot_base + h * (S::kG / GROUP);
+            m[h] = __shfl_sync(0xffffffffu, m_own, src);
+            l[h] = __shfl_sync(0xffffffffu, l_own, src);
+        }
     }
     if (*flag) {
         // A wait gave up: drain this warp's copies still in flight (bounded)
@@ -659,6 +742,52 @@ DecodeKernel select_decode(const InferlabCudaKvPool& pool, std::uint32_t group, 
     return pick_kernel<__nv_bfloat16>(pool.head_dim, group, smem);
 }
 
+// CTAs of `kernel` resident per SM times the SMs of `device` (cached per
+// kernel and device; 0 when unknown).
+std::uint32_t resident_slots(DecodeKernel kernel, std::size_t smem, int device) {
+    static std::mutex mutex;
+    static std::map<std::pair<const void*, int>, std::uint32_t> cache;
+    std::lock_guard<std::mutex> lock(mutex);
+    const auto key = std::make_pair(reinterpret_cast<const void*>(kernel), device);
+    const auto found = cache.find(key);
+    if (found != cache.end()) return found->second;
+    int per_sm = 0, sms = 0;
+    std::uint32_t slots = 0;
+    if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(smem)) == cudaSuccess &&
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, kDecodeWarps * 32, smem) ==
+            cudaSuccess &&
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device) == cudaSuccess) {
+        slots = static_cast<std::uint32_t>(per_sm * sms);
+    } else {
+        cudaGetLastError();
+    }
+    cache.emplace(key, slots);
+    return slots;
+}
+
+// The split plan of a batch on this pool. One sequence (the split long
+// sequence, or a batch of one) is cut into as many equal splits as fill one
+// wave of resident CTAs exactly: a wave and a sliver (e.g. 64 splits x 8
+// kv-heads = 512 CTAs on 444 slots) would take two CTA durations.
+DecodePlan full_plan(const InferlabCudaKvPool& p, std::uint32_t num_seqs, std::uint32_t q_heads,
+                     std::uint32_t max_context_len) {
+    DecodePlan plan = plan_decode(num_seqs, p.kv_heads, max_context_len, p.decode_blocks_per_split);
+    if (num_seqs != 1 || p.decode_blocks_per_split != 0 || q_heads % p.kv_heads != 0) return plan;
+    std::size_t smem = 0;
+    DecodeKernel kernel = select_decode(p, q_heads / p.kv_heads, smem);
+    if (kernel == nullptr) return plan;
+    const std::uint32_t slots = resident_slots(kernel, smem, p.device);
+    if (slots == 0 || plan.max_splits * p.kv_heads <= slots) return plan;
+    const std::uint32_t max_blocks =
+        (max_context_len + kDecodeBlockTokens - 1) / kDecodeBlockTokens;
+    const std::uint32_t splits = std::min<std::uint32_t>(kMaxSplits, slots / p.kv_heads);
+    if (splits == 0) return plan;
+    const std::uint32_t bps = (max_blocks + splits - 1) / splits;
+    if (bps > static_cast<std::uint32_t>(kMaxBlocksPerSplit)) return plan;
+    return DecodePlan{bps, (max_blocks + bps - 1) / bps};
+}
+
 void validate_decode(const InferlabCudaKvPool& p, const float* queries,
                      const std::int32_t* block_tables, std::uint32_t max_blocks,
                      const std::int32_t* context_lens, std::uint32_t num_seqs,
@@ -742,8 +871,7 @@ void run_decode(InferlabCudaKvPool& p, const float* queries, const std::int32_t*
     if (reinterpret_cast<std::uintptr_t>(queries) % 16 != 0) {
         throw std::runtime_error("paged decode queries must be 16-byte aligned");
     }
-    const DecodePlan plan = plan_decode(num_seqs, p.kv_heads, max_context_len,
-                                        p.decode_blocks_per_split);
+    const DecodePlan plan = full_plan(p, num_seqs, q_heads, max_context_len);
     const std::size_t need = workspace_bytes_for(num_seqs, q_heads, p.kv_heads, p.head_dim, plan);
     if (plan.max_splits > 1 && (workspace == nullptr || workspace_bytes < need)) {
         throw std::runtime_error("paged decode workspace is too small");
@@ -795,8 +923,7 @@ namespace ilb {
 
 std::size_t decode_workspace_bytes(const InferlabCudaKvPool& pool, std::uint32_t num_seqs,
                                    std::uint32_t q_heads, std::uint32_t max_context_len) {
-    const auto plan = plan_decode(num_seqs, pool.kv_heads, max_context_len,
-                                  pool.decode_blocks_per_split);
+    const auto plan = full_plan(pool, num_seqs, q_heads, max_context_len);
     return workspace_bytes_for(num_seqs, q_heads, pool.kv_heads, pool.head_dim, plan);
 }
 
@@ -804,8 +931,7 @@ std::size_t decode_scratch_bytes(const InferlabCudaKvPool& pool, std::uint32_t n
                                  std::uint32_t q_heads, std::uint32_t max_context_len) {
     std::size_t smem = 0;
     if (select_decode(pool, q_heads / pool.kv_heads, smem) == nullptr) return 0;
-    const auto plan = plan_decode(num_seqs, pool.kv_heads, max_context_len,
-                                  pool.decode_blocks_per_split);
+    const auto plan = full_plan(pool, num_seqs, q_heads, max_context_len);
     if (plan.max_splits <= 1) return 0;
     return workspace_bytes_for(num_seqs, q_heads, pool.kv_heads, pool.head_dim, plan);
 }
@@ -839,8 +965,7 @@ extern "C" std::size_t inferlab_cuda_paged_decode_workspace_size(const InferlabC
                                                                  std::uint32_t max_context_len) {
     if (pool == nullptr || num_seqs == 0 || q_heads == 0 || max_context_len == 0) return 0;
     try {
-        const auto plan = ilb::plan_decode(num_seqs, pool->kv_heads, max_context_len,
-                                           pool->decode_blocks_per_split);
+        const auto plan = ilb::full_plan(*pool, num_seqs, q_heads, max_context_len);
         return ilb::workspace_bytes_for(num_seqs, q_heads, pool->kv_heads, pool->head_dim, plan);
     } catch (...) {
         return 0;  // the decode call itself reports why
