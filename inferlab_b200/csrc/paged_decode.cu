@@ -662,12 +662,14 @@ DecodePlan plan_decode(std::uint32_t num_seqs, std::uint32_t kv_heads,
         (max_context_len + kDecodeBlockTokens - 1) / kDecodeBlockTokens;
     std::uint32_t bps = fixed_blocks_per_split;
     if (bps == 0) {
-        // Aim for about six waves of two CTAs per SM across 148 SMs if every
-        // context were max_context_len long, with at least 8 blocks per split
-        // (measured on 64 x U[64, 2048] fp32: 26 blocks per split 4872 GB/s,
-        // 32 blocks 5064, 43 blocks 5007, 16 blocks 4808).
+        // Aim for about 2048 CTAs (4.6 waves of three CTAs per SM across 148
+        // SMs) if every context were max_context_len long, with at least 8
+        // blocks per split. Measured on 64 x U[64, 2048] fp32 (32 blocks per
+        // split best: 16 blocks 4% and 22-26 blocks 3% slower) and on the
+        // Zipf-skewed 32 x [32, 8192] bf16 GQA batch (64 blocks per split
+        // 98.4 us; 57 blocks 106.4, 74 blocks 104.4, 86 blocks 114.6).
         const std::uint64_t pairs = static_cast<std::uint64_t>(num_seqs) * kv_heads;
-        const std::uint64_t target = 148ull * 2 * 6;
+        const std::uint64_t target = 2048;
         std::uint64_t splits = (target + pairs - 1) / pairs;
         splits = std::max<std::uint64_t>(1, std::min<std::uint64_t>(splits, max_blocks));
         bps = static_cast<std::uint32_t>((max_blocks + splits - 1) / splits);
