@@ -301,9 +301,10 @@ int inferlab_cuda_paged_decode_noalloc(InferlabCudaKvPool* pool, const float* qu
  * inputs, and the decode writes straight into `out`: two launches and a
  * 4-byte copy. Otherwise the inputs cross to HBM by copies (through the
  * pool's pinned staging for pageable arrays), then kv_append, one decode
- * launch, one copy back. Waits at most timeout_ms (0 = 10 s). Block ids and
- * context lengths are checked on the host first (the reference's materialize
- * checks, :776-789).
+ * launch, one copy back. Waits at most timeout_ms (0 = 10 s). Context lengths
+ * are checked on the host first; block ids where the append and decode kernels
+ * read them, failing the call with the same message (the reference's
+ * materialize checks, :776-789).
  */
 int inferlab_cuda_decode_step_host(InferlabCudaKvPool* pool, const float* queries,
                                    const float* new_keys, const float* new_values,
