@@ -165,7 +165,7 @@ def test_decode_step_host_matches_device_calls(torch_mod, wl, oracle_mod):
     # the appended rows are in the pool at position ctx - 1
     kg, _ = batch.pool.gather(batch.block_tables[4, :128].contiguous(), 2048)
     assert torch.equal(kg[2047].cpu(), torch.from_numpy(k_new[4]).to(torch.bfloat16))
-    # host-side checks fire before any device work
+    # invalid block ids and context lengths fail the call with the reference's messages
     from inferlab_b200 import AttentionError
 
     bad = batch.tables_host.copy()
