@@ -204,19 +204,47 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, GROUP >= 8 ? 1 : 3)
     const int b0 = static_cast<int>(split) * bps;
     const int nb = min(nblk - b0, bps);
 
-    for (int i = threadIdx.x; i < nb; i += blockDim.x) {
+    // This warp's blocks: local index warp, warp + W, ...
+    const int my_count = warp < nb ? (nb - warp + kDecodeWarps - 1) / kDecodeWarps : 0;
+    unsigned char* tiles = smem + static_cast<std::size_t>(warp) * kDecodeStages * 2 * S::kTileBytes;
+    std::uint64_t* my_bars = bars + warp * kDecodeStages;
+    const std::size_t head_offset = static_cast<std::size_t>(kv_head) * S::kTileBytes;
+    const std::size_t block_stride = static_cast<std::size_t>(p.kv_heads) * S::kTileBytes;
+    // Physical block of the split's local block i (an id outside the pool is
+    // reported and replaced by block 0, never dereferenced).
+    auto block_id = [&](int i) {
         std::int32_t id = p.tables[static_cast<std::size_t>(seq) * p.max_blocks + b0 + i];
         if (id < 0 || static_cast<std::uint64_t>(id) >= p.num_blocks) {
             flag_error(p.error_word, kErrBadBlock);
             id = 0;
         }
-        ids[i] = id;
-    }
-    if (threadIdx.x == 0) {
-        for (int s = 0; s < kDecodeWarps * kDecodeStages; ++s) mbar_init(&bars[s], 1);
-        *flag = 0;
+        return id;
+    };
+    auto issue_block = [&](int j, std::int32_t id) {
+        const int stage = j % kDecodeStages;
+        const std::size_t src = static_cast<std::size_t>(id) * block_stride + head_offset;
+        unsigned char* dst = tiles + static_cast<std::size_t>(stage) * 2 * S::kTileBytes;
+        mbar_arrive_expect_tx(&my_bars[stage], 2 * S::kTileBytes);
+        bulk_copy_g2s(dst, p.key_arena + src, S::kTileBytes, &my_bars[stage]);
+        bulk_copy_g2s(dst + S::kTileBytes, p.value_arena + src, S::kTileBytes, &my_bars[stage]);
+    };
+    // Each warp starts its first copies at once: lane 0 initialises the
+    // warp's own barriers and reads those blocks' ids itself, before the CTA
+    // has read the rest of the split's table and the queries.
+    if (lane == 0) {
+        for (int st = 0; st < kDecodeStages; ++st) mbar_init(&my_bars[st], 1);
         fence_barrier_init();
+        std::int32_t first[kDecodeStages];
+        const int n_first = min(my_count, kDecodeStages);
+#pragma unroll
+        for (int j = 0; j < kDecodeStages; ++j) first[j] = j < n_first ? block_id(warp + j * kDecodeWarps) : 0;
+#pragma unroll
+        for (int j = 0; j < kDecodeStages; ++j) {
+            if (j < n_first) issue_block(j, first[j]);
+        }
     }
+    for (int i = threadIdx.x; i < nb; i += blockDim.x) ids[i] = block_id(i);
+    if (threadIdx.x == 0) *flag = 0;
     __syncthreads();
 
     // Queries of the GQA group, rounded to the pool type (the reference rounds
@@ -248,24 +276,7 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, GROUP >= 8 ? 1 : 3)
     }
     if (q_bad) flag_error(p.error_word, kErrNonFinite);
 
-    // This warp's blocks: local index warp, warp + W, ...
-    const int my_count = warp < nb ? (nb - warp + kDecodeWarps - 1) / kDecodeWarps : 0;
-    unsigned char* tiles = smem + static_cast<std::size_t>(warp) * kDecodeStages * 2 * S::kTileBytes;
-    std::uint64_t* my_bars = bars + warp * kDecodeStages;
-    const std::size_t head_offset = static_cast<std::size_t>(kv_head) * S::kTileBytes;
-    const std::size_t block_stride = static_cast<std::size_t>(p.kv_heads) * S::kTileBytes;
-    auto issue = [&](int j) {
-        const int stage = j % kDecodeStages;
-        const std::size_t src = static_cast<std::size_t>(ids[warp + j * kDecodeWarps]) * block_stride +
-                                head_offset;
-        unsigned char* dst = tiles + static_cast<std::size_t>(stage) * 2 * S::kTileBytes;
-        mbar_arrive_expect_tx(&my_bars[stage], 2 * S::kTileBytes);
-        bulk_copy_g2s(dst, p.key_arena + src, S::kTileBytes, &my_bars[stage]);
-        bulk_copy_g2s(dst + S::kTileBytes, p.value_arena + src, S::kTileBytes, &my_bars[stage]);
-    };
-    if (lane == 0) {
-        for (int j = 0; j < min(my_count, kDecodeStages); ++j) issue(j);
-    }
+    auto issue = [&](int j) { issue_block(j, ids[warp + j * kDecodeWarps]); };
 
     float m[GROUP];
     float l[GROUP];
