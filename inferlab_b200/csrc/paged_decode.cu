@@ -254,11 +254,15 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, GROUP >= 8 ? 1 : 3)
     // q and the accumulators are held as fp32 pairs (dims 2i, 2i + 1), so the
     // dot products and the P x V update take one f32x2 FMA per two dims: the
     // kernel is bound by instruction issue, not by the fp32 pipe.
+    // With the head-split softmax, slot i of a lane's q holds head
+    // i ^ own_head, so that every reduce-scatter round below keeps the lower
+    // half of the slots (no per-lane selects).
     std::uint64_t q2[GROUP][S::kDpl / 2];
+    const int own_head = S::kSplitHeads ? cg / (S::kG / GROUP) : 0;
     bool q_bad = false;
 #pragma unroll
     for (int h = 0; h < GROUP; ++h) {
-        const float* qrow = p.queries + (row0 + h) * D;
+        const float* qrow = p.queries + (row0 + (h ^ own_head)) * D;
 #pragma unroll
         for (int c = 0; c < S::kCh; ++c) {
             const int base = (cg + S::kG * c) * S::kEpc;
@@ -334,22 +338,21 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, GROUP >= 8 ? 1 : 3)
         if constexpr (S::kSplitHeads) {
             // Reduce-scatter over the heads: each round halves the heads a
             // lane holds, keeping the half with its own head (cg / kLph), then
-            // the kLph lanes of that head sum its scores. s[0] then holds this
+            // the kLph lanes of that head sum its scores. Slot i holds head
+            // i ^ own_head, so the kept half is always slots [0, n / 2) and the
+            // partner lane (own_head differing in the round's bit) sends the
+            // same heads from its slots [n / 2, n). s[0] then holds this
             // lane's own head.
             constexpr int kLph = S::kG / GROUP;
 #pragma unroll
             for (int k = 0; k < ilog2(GROUP); ++k) {
                 const int n = GROUP >> k;
                 const int off = S::kG >> (k + 1);
-                const bool upper = (cg & off) != 0;
 #pragma unroll
                 for (int i = 0; i < n / 2; ++i) {
 #pragma unroll
                     for (int r = 0; r < S::kR; ++r) {
-                        const float lo_v = s[i][r];
-                        const float hi_v = s[i + n / 2][r];
-                        const float keep = upper ? hi_v : lo_v;
-                        s[i][r] = keep + __shfl_xor_sync(0xffffffffu, upper ? lo_v : hi_v, off);
+                        s[i][r] += __shfl_xor_sync(0xffffffffu, s[i + n / 2][r], off);
                     }
                 }
             }
