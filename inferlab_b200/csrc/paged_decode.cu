@@ -17,7 +17,9 @@
 //  * lanes split as (token slot, 16-byte chunk group): kG lanes share one
 //    token row, each holding kDpl dims of every q-head of the GQA group in
 //    registers; dot products reduce with kG-wide xor shuffles; every token
-//    slot keeps its own online-softmax state (m, l, acc) in the log2 domain.
+//    slot keeps its own online-softmax state (m, l, acc) in the log2 domain,
+//    its kept max moving only when exceeded by more than 2^8 (the
+//    accumulators are rescaled only then).
 //  * at the end the slot states merge by shuffles, the warps by shared
 //    memory, and - when the context was split - the CTAs by a fused
 //    log-sum-exp combine: every CTA writes (m, l, acc) to the workspace, and
@@ -49,6 +51,11 @@ constexpr int kMaxBlocksPerSplit = 1024;
 constexpr std::uint32_t kMaxSplits = 64;
 
 constexpr int ilog2(int x) { return x <= 1 ? 0 : 1 + ilog2(x / 2); }
+// Lazy rescale (log2 units): a running max moves only when a block's max
+// exceeds it by more than 2^8, so probabilities relative to the kept max stay
+// <= 256 (no fp32 overflow) and the accumulators are rescaled only then - the
+// same online-softmax recurrence (kernels/attention_cpu.cpp:364-386).
+constexpr float kDecodeRescale = 8.0f;
 
 template <typename KvT, int D, int GROUP>
 struct DecodeShape {
@@ -368,9 +375,13 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, GROUP >= 8 ? 1 : 3)
                 mx = fmaxf(mx, s[0][r]);
             }
             const float m_new = fmaxf(m_own, mx);
-            const float base = safe_max(m_new);
-            const float alpha_own = exp2f(m_own - base);
-            m_own = m_new;
+            const bool grow = m_new > m_own + kDecodeRescale;
+            float alpha_own = 1.0f;
+            if (grow) {
+                alpha_own = exp2f(m_own - m_new);
+                m_own = m_new;
+            }
+            const float base = safe_max(m_own);
             float sum = 0.0f;
 #pragma unroll
             for (int r = 0; r < S::kR; ++r) {
@@ -378,17 +389,23 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, GROUP >= 8 ? 1 : 3)
                 sum += s[0][r];
             }
             l_own = l_own * alpha_own + sum;
-            // Every head's probabilities and rescale factor from its lanes.
+            // Every head's probabilities (and, when some head's max moved, its
+            // rescale factor) from its lanes.
+            if (__any_sync(0xffffffffu, grow)) {
+#pragma unroll
+                for (int h = 0; h < GROUP; ++h) {
+                    const float alpha = __shfl_sync(0xffffffffu, alpha_own, slot_base + h * kLph);
+                    const std::uint64_t alpha2 = pack_f32x2(alpha, alpha);
+#pragma unroll
+                    for (int e = 0; e < S::kDpl / 2; ++e) acc2[h][e] = mul2(acc2[h][e], alpha2);
+                }
+            }
             float p_all[GROUP][S::kR];
 #pragma unroll
             for (int h = 0; h < GROUP; ++h) {
                 const int src = slot_base + h * kLph;
-                const float alpha = __shfl_sync(0xffffffffu, alpha_own, src);
 #pragma unroll
                 for (int r = 0; r < S::kR; ++r) p_all[h][r] = __shfl_sync(0xffffffffu, s[0][r], src);
-                const std::uint64_t alpha2 = pack_f32x2(alpha, alpha);
-#pragma unroll
-                for (int e = 0; e < S::kDpl / 2; ++e) acc2[h][e] = mul2(acc2[h][e], alpha2);
             }
 #pragma unroll
             for (int h = 0; h < GROUP; ++h) {
@@ -413,9 +430,13 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, GROUP >= 8 ? 1 : 3)
                     mx = fmaxf(mx, s[h][r]);
                 }
                 const float m_new = fmaxf(m[h], mx);
-                const float base = safe_max(m_new);
-                const float alpha = exp2f(m[h] - base);
-                m[h] = m_new;
+                const bool grow = m_new > m[h] + kDecodeRescale;
+                float alpha = 1.0f;
+                if (grow) {
+                    alpha = exp2f(m[h] - m_new);
+                    m[h] = m_new;
+                }
+                const float base = safe_max(m[h]);
                 float sum = 0.0f;
     #pragma unroll
                 for (int r = 0; r < S::kR; ++r) {
@@ -423,15 +444,20 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, GROUP >= 8 ? 1 : 3)
                     sum += s[h][r];
                 }
                 l[h] = l[h] * alpha + sum;
-                const std::uint64_t alpha2 = pack_f32x2(alpha, alpha);
+                if (__any_sync(0xffffffffu, grow)) {
+                    const std::uint64_t alpha2 = pack_f32x2(alpha, alpha);
     #pragma unroll
-                for (int e = 0; e < S::kDpl / 2; ++e) acc2[h][e] = mul2(acc2[h][e], alpha2);
+                    for (int e = 0; e < S::kDpl / 2; ++e) acc2[h][e] = mul2(acc2[h][e], alpha2);
+                }
             }
         }
 #pragma unroll
         for (int r = 0; r < S::kR; ++r) {
             const int trow = ts + S::kTS * r;
             if (trow >= valid) continue;
+            std::uint64_t p2[GROUP];
+#pragma unroll
+            for (int h = 0; h < GROUP; ++h) p2[h] = pack_f32x2(s[h][r], s[h][r]);
 #pragma unroll
             for (int c = 0; c < S::kCh; ++c) {
                 const uint4 raw = *reinterpret_cast<const uint4*>(
@@ -440,7 +466,7 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, GROUP >= 8 ? 1 : 3)
                 widen16_pairs(raw, v2, KvT{});
 #pragma unroll
                 for (int h = 0; h < GROUP; ++h) {
-                    const std::uint64_t s2 = pack_f32x2(s[h][r], s[h][r]);
+                    const std::uint64_t s2 = p2[h];
 #pragma unroll
                     for (int e = 0; e < S::kEpc / 2; ++e) {
                         acc2[h][c * S::kEpc / 2 + e] = fma2(s2, v2[e], acc2[h][c * S::kEpc / 2 + e]);
