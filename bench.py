@@ -268,19 +268,26 @@ def cpu_model() -> str:
 
 
 def timed_region(args, dist, device, stream, flush, parts):
-    """Untimed 0.5 s pre-roll of the step (so the clock samples see the GPU
-    under this load), then exactly args.steps steps, each part bracketed by its
-    own CUDA events on `stream`, with the L2 flushed before every step; a
-    barrier and a device synchronize on both sides. Returns each part's total
-    milliseconds on this rank."""
+    """Untimed pre-roll of about 0.5 s of the step (so the clock samples see
+    the GPU under this load), then exactly args.steps steps, each part
+    bracketed by its own CUDA events on `stream`, with the L2 flushed before
+    every step; a barrier and a device synchronize on both sides. Every rank
+    runs the same number of pre-roll steps (sized from the slowest rank's
+    first step), since a step may hold collectives or peer exchanges that pair
+    up across ranks. Returns each part's total milliseconds on this rank."""
     import torch
 
-    preroll_end = time.perf_counter() + 0.5
-    while time.perf_counter() < preroll_end:
+    def one_step():
         flush.fill_(0.0)
         for part in parts:
             part()
         stream.synchronize()
+
+    start = time.perf_counter()
+    one_step()
+    first = max_over_ranks(dist, time.perf_counter() - start)
+    for _ in range(max(0, min(int(0.5 / max(first, 1e-6)), 20000) - 1)):
+        one_step()
     events = [[(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
                for _ in parts] for _ in range(args.steps)]
     barrier(dist)
@@ -689,9 +696,11 @@ def measure_prefill(args, dist, world, rank, device, peaks, peak_kind):
 # ---------------------------------------------------------------------------
 def measure_long_sequence(args, dist, world, rank, device, peaks, peak_kind):
     """One 131072-token sequence split across the ranks: per step, decode
-    partials over the local blocks into one packed [m | l | o] block, one NCCL
-    all-gather of the blocks, rank-order log-sum-exp merge. Timed per rank with
-    events, max over ranks."""
+    partials over the local blocks into one packed [m | l | o] block, then (at
+    N > 1) one kernel that stores the block into every peer's receive buffer
+    over NVLink, waits for all ranks' blocks and merges them in rank order
+    (distributed.PeerExchange). The NCCL all-gather + merge of the same
+    partials is timed beside it. Timed per rank with events, max over ranks."""
     import torch
 
     from inferlab_b200 import distributed, workloads as wl
@@ -703,17 +712,42 @@ def measure_long_sequence(args, dist, world, rank, device, peaks, peak_kind):
     local = int(batch.contexts[0])
     workspace = pool.make_workspace(1, 32, local)
 
+    exchange, exchange_error = None, None
+    if world > 1:
+        try:
+            exchange = distributed.PeerExchange(32, 128)
+        except (RuntimeError, ValueError) as caught:  # every rank takes this branch together
+            exchange_error = str(caught)
+
     def step():
+        return distributed.decode_split_sequence(pool, batch.queries, batch.block_tables, local,
+                                                 workspace=workspace, exchange=exchange)
+
+    def step_nccl():
         return distributed.decode_split_sequence(pool, batch.queries, batch.block_tables, local,
                                                  workspace=workspace)
 
     for i in range(args.warmup):
         flush.fill_(float(i))
         step()
+        if exchange is not None:
+            step_nccl()
     pool.synchronize()
     with ClockSampler(device) as clocks:
         (ms,) = timed_region(args, dist, device, stream, flush, [step])
     pool.synchronize()
+    nccl = None
+    if exchange is not None:
+        exchange.synchronize(timeout_ms=20000)  # raises if a peer's block never arrived
+        (nccl_ms,) = timed_region(args, dist, device, stream, flush, [step_nccl])
+        pool.synchronize()
+        nccl_total = max_over_ranks(dist, nccl_ms)
+        nccl = {"ms_per_step": round(nccl_total / args.steps, 5),
+                "value": round(131072 * 8 * 128 * 2 * 2 * args.steps / (nccl_total * 1e-3) / 1e9, 3),
+                "unit": "GB/s",
+                "path": "the same partials exchanged by all_gather_into_tensor over NCCL, "
+                        "then inferlab_cuda_lse_combine_packed"}
+        exchange.close()
     total_ms = max_over_ranks(dist, ms)
     kv_bytes = 131072 * 8 * 128 * 2 * 2
     value = kv_bytes * args.steps / (total_ms * 1e-3) / 1e9
@@ -727,18 +761,26 @@ def measure_long_sequence(args, dist, world, rank, device, peaks, peak_kind):
         "ms_per_step": round(total_ms / args.steps, 5), "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded)",
         "config": {"workload": "one 131072-token sequence, GQA 32/8 x 128 bf16, blocks split "
-                               "across GPUs, NCCL all-gather of (m, l, o) + rank-order merge",
+                               "across GPUs, (m, l, o) partials exchanged and merged in rank order"
+                               + (" in one kernel over NVLink peer memory" if exchange is not None
+                                  else ""),
                    "tokens_this_rank": local, "comm_nranks": comm,
-                   "collective": ("all_gather_into_tensor over NCCL, "
-                                  f"{32 * 130 * 4} B per rank" if comm else "none (one GPU)"),
+                   "collective": ("peer stores over NVLink inside the merge kernel "
+                                  "(inferlab_cuda_peer_exchange_combine), "
+                                  f"{32 * 130 * 4} B from every rank to every peer, flags per step"
+                                  if exchange is not None else
+                                  f"all_gather_into_tensor over NCCL ({exchange_error})"
+                                  if comm and comm > 1 else "none (one GPU)"),
                    "l2": L2_NOTE},
         "roofline": {"bound": "hbm", "achieved_per_gpu": round(value / world, 2),
                      "peak": peaks["hbm_gbs"], "unit": "GB/s",
                      "frac": round(value / world / peaks["hbm_gbs"], 4),
                      "peak_kind": f"{peak_kind} hbm_gbs"},
-        "gpu_launches": (3 if world > 1 else 2) * args.steps, "clocks": clock,
+        "gpu_launches": 2 * args.steps, "clocks": clock,
         "per_rank": per_rank(dist, ms_per_step=ms / args.steps, sm_mhz=clock["sm_mhz"]),
     }
+    if nccl is not None:
+        line["nccl_all_gather"] = nccl
     pool.close()
     return line
 

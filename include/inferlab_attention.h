@@ -497,6 +497,58 @@ int inferlab_cuda_pages_stats(InferlabCudaPageManager* manager, InferlabPagedCac
 int inferlab_cuda_pages_copy(InferlabCudaKvPool* pool, const int32_t* from, const int32_t* to,
                              uint32_t count, void* stream, char* error, size_t error_capacity);
 
+/*
+ * Peer exchange of split-KV partials (one process per GPU, GPUs of one box
+ * connected by NVLink): the all-gather of the packed [m | l | o] blocks and
+ * inferlab_cuda_lse_combine_packed in ONE kernel. Each rank allocates its
+ * receive buffer (inferlab_cuda_peer_buffer_alloc, which also returns the
+ * buffer's CUDA IPC handle), the ranks swap handles over their own process
+ * group, and inferlab_cuda_peer_exchange_create opens the peers' buffers.
+ * Per call the kernel stores this rank's block into slot `rank` of every
+ * peer's buffer (peer stores over NVLink, no multicast), raises this step's
+ * flag in each peer's buffer, waits (bounded, ~2 s) until every rank's flag
+ * for this step has arrived in its own buffer, and merges the blocks in rank
+ * order, bit for bit as inferlab_cuda_lse_combine_packed would. Blocks and
+ * flags alternate between two slots by step parity, so a rank one step ahead
+ * never overwrites a block a peer is still merging. A wait that gives up
+ * records "device wait timed out", read by inferlab_cuda_peer_exchange_synchronize.
+ * Every rank must call the same sequence of exchanges; no reference
+ * counterpart (the reference has no split-sequence decode).
+ */
+typedef struct InferlabCudaPeerExchange InferlabCudaPeerExchange;
+
+#define INFERLAB_CUDA_IPC_HANDLE_BYTES 64u
+#define INFERLAB_CUDA_PEER_MAX_RANKS 8u
+
+/* Bytes of one rank's receive buffer for `world` ranks and `rows` rows. */
+uint64_t inferlab_cuda_peer_buffer_bytes(uint32_t world, uint64_t rows, uint32_t head_dim);
+
+/* Allocates and zeroes a receive buffer on `device`; writes its IPC handle
+ * (INFERLAB_CUDA_IPC_HANDLE_BYTES bytes) to handle. */
+int inferlab_cuda_peer_buffer_alloc(int device, uint64_t bytes, void** buffer, void* handle,
+                                    char* error, size_t error_capacity);
+int inferlab_cuda_peer_buffer_free(int device, void* buffer, char* error, size_t error_capacity);
+
+/* handles: world x INFERLAB_CUDA_IPC_HANDLE_BYTES, rank r's at r (this rank's
+ * own entry is ignored); local_buffer: this rank's buffer. */
+int inferlab_cuda_peer_exchange_create(int device, uint32_t world, uint32_t rank, uint64_t rows,
+                                       uint32_t head_dim, void* local_buffer, const void* handles,
+                                       InferlabCudaPeerExchange** out, char* error,
+                                       size_t error_capacity);
+
+/* packed: this rank's [m | l | o] block (rows x (head_dim + 2) fp32, device);
+ * out: [rows][head_dim] fp32 (device). Asynchronous on `stream`. */
+int inferlab_cuda_peer_exchange_combine(InferlabCudaPeerExchange* exchange, const float* packed,
+                                        float* out, void* stream, char* error,
+                                        size_t error_capacity);
+
+/* Waits for `stream` (bounded) and reports a device-detected wait timeout. */
+int inferlab_cuda_peer_exchange_synchronize(InferlabCudaPeerExchange* exchange, void* stream,
+                                            uint32_t timeout_ms, char* error, size_t error_capacity);
+
+/* Closes the peers' buffers; every rank must have finished its exchanges. */
+void inferlab_cuda_peer_exchange_destroy(InferlabCudaPeerExchange* exchange);
+
 /* Library version string, e.g. "inferlab-b200 0.1 sm_100a". */
 const char* inferlab_cuda_version(void);
 

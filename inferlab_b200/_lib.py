@@ -90,6 +90,18 @@ SIGNATURES = {
         ctypes.c_int32, ctypes.c_uint32, ctypes.c_uint64, ctypes.c_uint32, ctypes.c_uint32,
         ctypes.c_uint32, ctypes.POINTER(c_vp), c_err, c_sz]),
     "inferlab_cuda_pool_destroy": (None, [c_vp]),
+    "inferlab_cuda_peer_buffer_bytes": (ctypes.c_uint64, [ctypes.c_uint32, ctypes.c_uint64,
+                                                          ctypes.c_uint32]),
+    "inferlab_cuda_peer_buffer_alloc": (ctypes.c_int, [
+        ctypes.c_int, ctypes.c_uint64, ctypes.POINTER(c_vp), c_vp, c_err, c_sz]),
+    "inferlab_cuda_peer_buffer_free": (ctypes.c_int, [ctypes.c_int, c_vp, c_err, c_sz]),
+    "inferlab_cuda_peer_exchange_create": (ctypes.c_int, [
+        ctypes.c_int, ctypes.c_uint32, ctypes.c_uint32, ctypes.c_uint64, ctypes.c_uint32, c_vp,
+        c_vp, ctypes.POINTER(c_vp), c_err, c_sz]),
+    "inferlab_cuda_peer_exchange_combine": (ctypes.c_int, [c_vp, c_vp, c_vp, c_vp, c_err, c_sz]),
+    "inferlab_cuda_peer_exchange_synchronize": (ctypes.c_int, [
+        c_vp, c_vp, ctypes.c_uint32, c_err, c_sz]),
+    "inferlab_cuda_peer_exchange_destroy": (None, [c_vp]),
     "inferlab_cuda_pool_info": (ctypes.c_int, [
         c_vp, ctypes.POINTER(InferlabCudaPoolInfo), c_err, c_sz]),
     "inferlab_cuda_pool_synchronize": (ctypes.c_int, [c_vp, c_vp, ctypes.c_uint32, c_err, c_sz]),

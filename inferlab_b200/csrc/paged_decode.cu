@@ -30,6 +30,7 @@
 #include "common.cuh"
 #include "generic_attention.cuh"
 #include "internal.cuh"
+#include "lse_merge.cuh"
 #include "pool.cuh"
 
 #include "../../include/inferlab_attention.h"
@@ -669,26 +670,9 @@ __global__ void lse_combine_kernel(const float* part_m, const float* part_l, con
                                    std::uint64_t stride_o, float* out) {
     const std::uint64_t row = static_cast<std::uint64_t>(blockIdx.x) * (blockDim.x / 32) +
                               threadIdx.x / 32;
-    const int lane = threadIdx.x & 31;
     if (row >= rows) return;
-    float mw = -INFINITY;
-    for (std::uint32_t i = 0; i < parts; ++i) {
-        if (part_l[i * stride_l + row] > 0.0f) mw = fmaxf(mw, part_m[i * stride_m + row]);
-    }
-    float lsum = 0.0f;
-    for (std::uint32_t i = 0; i < parts; ++i) {
-        const float li = part_l[i * stride_l + row];
-        if (li > 0.0f) lsum += li * expf(part_m[i * stride_m + row] - mw);
-    }
-    for (std::uint32_t dim = lane; dim < head_dim; dim += 32) {
-        float a = 0.0f;
-        for (std::uint32_t i = 0; i < parts; ++i) {
-            if (part_l[i * stride_l + row] > 0.0f) {
-                a += part_o[i * stride_o + row * head_dim + dim] * expf(part_m[i * stride_m + row] - mw);
-            }
-        }
-        out[row * head_dim + dim] = a / lsum;
-    }
+    lse_merge_row(part_m, part_l, part_o, parts, row, head_dim, stride_m, stride_l, stride_o, out,
+                  threadIdx.x & 31);
 }
 
 struct DecodePlan {

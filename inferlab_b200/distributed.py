@@ -11,7 +11,8 @@ Two ways the work spreads over the GPUs of one box:
   (inferlab_cuda_paged_decode_partials), the partials are all-gathered over
   the process group (NCCL on GPUs, gloo in the CPU tests) and merged in rank
   order (inferlab_cuda_lse_combine), which makes the result independent of
-  arrival order.
+  arrival order; on GPUs `PeerExchange` does the exchange and the merge in one
+  kernel over NVLink peer memory instead.
 """
 from __future__ import annotations
 
@@ -67,15 +68,130 @@ def all_gather_partials(m, l, o, group=None):
     return tuple(out)
 
 
-def decode_split_sequence(pool, queries, block_table, local_len: int, group=None, workspace=None):
+class PeerExchange:
+    """The all-gather of packed [m | l | o] partials and their rank-order merge
+    in one kernel over NVLink peer memory (inferlab_cuda_peer_exchange_*): each
+    rank's receive buffer is opened by its peers through CUDA IPC handles swapped
+    over the process group once; per call the kernel stores this rank's block
+    into every peer's buffer, raises that step's flag there, waits (bounded) for
+    all ranks' flags and merges. One process per GPU, every rank on its own GPU
+    (ranks sharing a GPU would wait on each other from separate launches), and
+    every rank makes the same sequence of calls. Setting up is collective and
+    agreed: if any rank cannot allocate or open a buffer, every rank raises
+    RuntimeError (and holds nothing), so callers can fall back together."""
+
+    def __init__(self, rows: int, head_dim: int, group=None):
+        import ctypes
+
+        import torch
+        import torch.distributed as dist
+
+        from . import _lib
+        from .paged import _check
+
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.rows, self.head_dim = int(rows), int(head_dim)
+        self.device = torch.cuda.current_device()
+        self._lib = _lib.lib()
+        if self.world > 8:
+            raise ValueError("the peer exchange covers up to 8 ranks")
+        uuids = [None] * self.world
+        dist.all_gather_object(uuids, str(torch.cuda.get_device_properties(self.device).uuid),
+                               group=group)
+        if len(set(uuids)) != self.world:
+            raise ValueError("the peer exchange needs one GPU per rank")
+        def agree(ok: bool) -> bool:
+            flag = torch.tensor([1 if ok else 0], dtype=torch.int32, device=f"cuda:{self.device}")
+            dist.all_reduce(flag, op=dist.ReduceOp.MIN, group=group)
+            return bool(flag.item())
+
+        nbytes = self._lib.inferlab_cuda_peer_buffer_bytes(self.world, self.rows, self.head_dim)
+        handle = ctypes.create_string_buffer(64)
+        self._buffer = ctypes.c_void_p()
+        self._handle = None
+        error = _lib.error_buffer()
+        status = self._lib.inferlab_cuda_peer_buffer_alloc(self.device, nbytes, ctypes.byref(self._buffer),
+                                                           handle, error, len(error))
+        if not agree(status == 0):
+            if status == 0:
+                self._lib.inferlab_cuda_peer_buffer_free(self.device, self._buffer, error, len(error))
+            raise RuntimeError("peer exchange buffers could not be allocated on every rank: "
+                               + error.value.decode())
+        handles = [None] * self.world
+        dist.all_gather_object(handles, handle.raw, group=group)
+        joined = ctypes.create_string_buffer(b"".join(handles), 64 * self.world)
+        made = ctypes.c_void_p()
+        status = self._lib.inferlab_cuda_peer_exchange_create(
+            self.device, self.world, self.rank, self.rows, self.head_dim, self._buffer, joined,
+            ctypes.byref(made), error, len(error))
+        if not agree(status == 0):
+            if status == 0:
+                self._lib.inferlab_cuda_peer_exchange_destroy(made)
+            dist.barrier(group=group)  # no rank still holds a peer's buffer open
+            self._lib.inferlab_cuda_peer_buffer_free(self.device, self._buffer, error, len(error))
+            raise RuntimeError("peer exchange buffers could not be opened on every rank: "
+                               + error.value.decode())
+        self._handle = made
+        dist.barrier(group=group)  # every rank's buffer is open before the first push
+
+    def combine(self, packed, out=None, stream=None):
+        """Merged [rows, head_dim] output of every rank's packed block (this
+        rank's is `packed`); asynchronous on the current stream."""
+        import torch
+
+        from . import _lib
+        from .paged import _check, _stream_handle, _vp
+
+        if out is None:
+            out = torch.empty((self.rows, self.head_dim), dtype=torch.float32, device=packed.device)
+        error = _lib.error_buffer()
+        _check(self._lib.inferlab_cuda_peer_exchange_combine(
+            self._handle, _vp(packed), _vp(out), _stream_handle(self.device, stream), error,
+            len(error)), error)
+        return out
+
+    def synchronize(self, stream=None, timeout_ms: int = 0) -> None:
+        """Waits for the stream and raises if a peer's block never arrived."""
+        from . import _lib
+        from .paged import _check, _stream_handle
+
+        error = _lib.error_buffer()
+        _check(self._lib.inferlab_cuda_peer_exchange_synchronize(
+            self._handle, _stream_handle(self.device, stream), int(timeout_ms), error, len(error)),
+            error)
+
+    def close(self) -> None:
+        """Releases the peers' buffers and this rank's (after every rank's last
+        exchange: a barrier first)."""
+        import torch
+        import torch.distributed as dist
+
+        from . import _lib
+
+        if self._handle is None:
+            return
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)
+        self._lib.inferlab_cuda_peer_exchange_destroy(self._handle)
+        self._handle = None
+        dist.barrier(group=self.group)  # no peer still holds this rank's buffer open
+        error = _lib.error_buffer()
+        self._lib.inferlab_cuda_peer_buffer_free(self.device, self._buffer, error, len(error))
+
+
+def decode_split_sequence(pool, queries, block_table, local_len: int, group=None, workspace=None,
+                          exchange: PeerExchange | None = None):
     """Decode one query per row against a sequence whose blocks are spread
     over the ranks: this rank's blocks are `block_table` (device int32
     [rows, blocks]) covering `local_len` tokens. Returns the merged output
     [rows, q_heads, head_dim] on every rank.
 
-    The partials are written straight into one packed [m | l | o] block, the
-    blocks of all ranks are exchanged with a single all-gather (NCCL), and
-    one kernel merges them in rank order."""
+    The partials are written straight into one packed [m | l | o] block; with
+    `exchange` one kernel pushes it to every peer over NVLink and merges all
+    ranks' blocks in rank order, otherwise the blocks of all ranks are
+    exchanged with a single all-gather (NCCL) and one kernel merges them."""
     import torch
     import torch.distributed as dist
 
@@ -92,6 +208,8 @@ def decode_split_sequence(pool, queries, block_table, local_len: int, group=None
     else:
         send[:nrows].fill_(float("-inf"))
         send[nrows:].zero_()
+    if exchange is not None:
+        return exchange.combine(send).view(rows, q_heads, hd)
     if world > 1:
         recv = torch.empty(world * send.numel(), dtype=torch.float32, device=queries.device)
         dist.all_gather_into_tensor(recv, send, group=group)

@@ -4,8 +4,10 @@ One 131,072-token sequence (GQA 32/8 x 128, bf16) split across the GPUs by
 contiguous block ranges: each rank decodes its range into (m, l, o)
 partials, the partials are all-gathered over NCCL and merged in rank order;
 the result must equal the whole-context decode on one GPU within the fp32
-tolerance |a - b| <= 1e-6 + 1e-5 |b|. Ranks are spawned processes with a
-short process-group timeout.
+tolerance |a - b| <= 1e-6 + 1e-5 |b|. The same partials exchanged and merged
+in one kernel over NVLink peer memory (distributed.PeerExchange, five calls
+in a row so both buffer parities are reused) must equal the NCCL result bit
+for bit. Ranks are spawned processes with a short process-group timeout.
 """
 import datetime
 import os
@@ -44,10 +46,16 @@ def _rank_main(rank, world, port, path):
         lo, hi = distributed.local_tokens(total, 16, world, rank)
         blocks = full.block_tables[:, lo // 16:(hi + 15) // 16].contiguous()
         merged = distributed.decode_split_sequence(full.pool, full.queries, blocks, hi - lo)
+        exchange = distributed.PeerExchange(32, 128)
+        peer = [distributed.decode_split_sequence(full.pool, full.queries, blocks, hi - lo,
+                                                  exchange=exchange).clone() for _ in range(5)]
+        exchange.synchronize(timeout_ms=20000)
+        exchange.close()
         whole = full.pool.decode(full.queries, full.block_tables, full.context_lens, total)
         full.pool.synchronize()
         if rank == 0:
-            np.save(path, np.stack([merged.cpu().numpy(), whole.cpu().numpy()]))
+            np.save(path, np.stack([merged.cpu().numpy(), whole.cpu().numpy()] +
+                                   [x.cpu().numpy() for x in peer]))
         full.pool.close()
         dist.barrier()
     finally:
@@ -64,6 +72,8 @@ def test_split_sequence_over_nccl_matches_single_gpu(tmp_path, world):
     path = str(tmp_path / "out.npy")
     mp.start_processes(_rank_main, args=(world, _port(), path), nprocs=world,
                        start_method="spawn", join=True)
-    merged, whole = np.load(path)
+    merged, whole, *peer = np.load(path)
     err = np.abs(merged.astype(np.float64) - whole)
     assert np.all(err <= 1e-6 + 1e-5 * np.abs(whole)), float(err.max())
+    for x in peer:
+        assert np.array_equal(x, merged)
