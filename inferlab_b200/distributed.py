@@ -181,6 +181,10 @@ class PeerExchange:
         self._lib.inferlab_cuda_peer_buffer_free(self.device, self._buffer, error, len(error))
 
 
+# Per (device, rows, local length): the constant lengths tensor of the split decode.
+_LENGTHS: dict = {}
+
+
 def decode_split_sequence(pool, queries, block_table, local_len: int, group=None, workspace=None,
                           exchange: PeerExchange | None = None):
     """Decode one query per row against a sequence whose blocks are spread
@@ -202,7 +206,11 @@ def decode_split_sequence(pool, queries, block_table, local_len: int, group=None
     world = dist.get_world_size(group) if dist.is_initialized() else 1
     send = torch.empty(nrows * (hd + 2), dtype=torch.float32, device=queries.device)
     if local_len > 0:
-        lens = torch.full((rows,), local_len, dtype=torch.int32, device=queries.device)
+        key = (queries.device.index, rows, local_len)
+        lens = _LENGTHS.get(key)
+        if lens is None:  # made once: a fill kernel per call would sit in every step
+            lens = _LENGTHS[key] = torch.full((rows,), local_len, dtype=torch.int32,
+                                              device=queries.device)
         pool.decode_partials(queries, block_table, lens, local_len, workspace=workspace,
                              packed=send)
     else:
