@@ -505,13 +505,14 @@ int inferlab_cuda_pages_copy(InferlabCudaKvPool* pool, const int32_t* from, cons
  * buffer's CUDA IPC handle), the ranks swap handles over their own process
  * group, and inferlab_cuda_peer_exchange_create opens the peers' buffers.
  * Per call the kernel stores this rank's block into slot `rank` of every
- * peer's buffer (peer stores over NVLink, no multicast), raises this step's
- * flag in each peer's buffer, waits (bounded, ~2 s) until every rank's flag
- * for this step has arrived in its own buffer, and merges the blocks in rank
- * order, bit for bit as inferlab_cuda_lse_combine_packed would. Blocks and
- * flags alternate between two slots by step parity, so a rank one step ahead
- * never overwrites a block a peer is still merging. A wait that gives up
- * records "device wait timed out", read by inferlab_cuda_peer_exchange_synchronize.
+ * peer's buffer (peer stores over NVLink, no multicast; every element as one
+ * 8-byte word with the step number in its high half, so no separate flag or
+ * fence is needed), waits (bounded, ~2 s) until every rank's words of this
+ * step have arrived in its own buffer, and merges the blocks in rank order,
+ * bit for bit as inferlab_cuda_lse_combine_packed would. The words alternate
+ * between two slots by step parity, so a rank one step ahead never overwrites
+ * a block a peer is still reading. A wait that gives up records "device wait
+ * timed out", read by inferlab_cuda_peer_exchange_synchronize.
  * Every rank must call the same sequence of exchanges; no reference
  * counterpart (the reference has no split-sequence decode).
  */

@@ -8,14 +8,17 @@
 // Instead of an NCCL all-gather followed by a merge launch, each rank's
 // kernel stores its packed [m | l | o] block straight into every peer's
 // receive buffer (plain peer stores through NVSwitch; no multicast, no
-// library kernel touches peer memory), raises a per-step flag there, waits
-// for all ranks' flags in its own buffer and merges in rank order with the
-// same per-row code as inferlab_cuda_lse_combine_packed.
+// library kernel touches peer memory) and merges all ranks' blocks in rank
+// order with the same per-row code as inferlab_cuda_lse_combine_packed.
 //
-// Receive buffer of one rank: blocks [2 parities][world][rows * (D + 2)] fp32,
-// then flags [2 parities][world] u32. Step s uses parity s & 1: a rank's push
-// of step s + 2 into a peer happens only after its own exchange s + 1 saw that
-// peer's step s + 1 flag, which that peer raised only after merging step s.
+// Every element travels as one aligned 8-byte store: its 32 bits in the low
+// half, the step number in the high half. An aligned 8-byte store is
+// single-copy atomic, so a receiver that reads the current step in a word
+// also reads that step's value: no flag and no system-scope fence between
+// data and flag. Receive buffer of one rank: words [2 parities][world][rows *
+// (D + 2)]. Step s uses parity s & 1: a rank pushes step s + 2 into a peer
+// only after its own exchange s + 1 has read that peer's step s + 1 words,
+// which the peer wrote only after its exchange s had read its step s words.
 #include "common.cuh"
 #include "lse_merge.cuh"
 
@@ -29,32 +32,31 @@ namespace {
 
 constexpr std::uint32_t kMaxRanks = INFERLAB_CUDA_PEER_MAX_RANKS;
 constexpr int kExchangeThreads = 256;
-// Bounded wait for a peer's flag: about 2^25 polls of >= 64 ns (> 2 s).
-constexpr std::uint32_t kFlagPolls = 1u << 25;
+// Bounded wait for the peers' words: at most 2^25 polls of >= 64 ns per
+// thread (> 2 s), shared by all the words the thread receives.
+constexpr std::uint32_t kWordPolls = 1u << 25;
 
 std::uint64_t align256(std::uint64_t n) { return (n + 255) & ~std::uint64_t(255); }
 
 struct BufferLayout {
     std::uint64_t block_floats;  // rows * (head_dim + 2)
-    std::uint64_t flags_offset;  // bytes
     std::uint64_t bytes;
 };
 
 BufferLayout buffer_layout(std::uint32_t world, std::uint64_t rows, std::uint32_t head_dim) {
     BufferLayout b{};
     b.block_floats = rows * (static_cast<std::uint64_t>(head_dim) + 2);
-    b.flags_offset = align256(2ull * world * b.block_floats * 4);
-    b.bytes = align256(b.flags_offset + 2ull * world * 4);
+    b.bytes = align256(2ull * world * b.block_floats * 8);
     return b;
 }
 
 struct ExchangeParams {
-    float* blocks[kMaxRanks];         // every rank's receive blocks (peer-mapped; own at [rank])
-    std::uint32_t* flags[kMaxRanks];  // every rank's flags
+    std::uint64_t* words[kMaxRanks];  // every rank's receive words (peer-mapped; own at [rank])
     const float* packed;              // this rank's block
     float* out;
     std::uint64_t rows;
     std::uint64_t block_floats;
+    std::uint32_t rows_per_cta;
     std::uint32_t head_dim;
     std::uint32_t world;
     std::uint32_t rank;
@@ -62,58 +64,103 @@ struct ExchangeParams {
     std::uint32_t* error_word;
 };
 
-__device__ __forceinline__ std::uint32_t load_acquire_sys(const std::uint32_t* p) {
-    std::uint32_t v;
-    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+__device__ __forceinline__ std::uint64_t load_word(const std::uint64_t* p) {
+    std::uint64_t v;
+    asm volatile("ld.volatile.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
     return v;
 }
 
-__device__ __forceinline__ void store_release_sys(std::uint32_t* p, std::uint32_t v) {
-    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-
-// CTA p stores this rank's block into rank p's buffer and raises this rank's
-// flag there; then every CTA waits for all flags of this step in its own
-// buffer and merges a share of the rows (one warp per row).
+// CTA c stores this rank's block into rank c's buffer, then receives rows
+// [c * R, (c + 1) * R) of every rank's block into shared memory and merges
+// them (one warp per row).
 __global__ void __launch_bounds__(kExchangeThreads) peer_exchange_kernel(const ExchangeParams p) {
+    extern __shared__ float parts[];  // [3][world][R] m, l then [world][R][D] o
     const std::uint32_t parity = p.step & 1u;
-    const std::uint32_t dst_rank = blockIdx.x;
+    const std::uint64_t tag = static_cast<std::uint64_t>(p.step) << 32;
     {
-        float* dst = p.blocks[dst_rank] + (static_cast<std::uint64_t>(parity) * p.world + p.rank) * p.block_floats;
-        if (p.block_floats % 4 == 0) {
-            const float4* src4 = reinterpret_cast<const float4*>(p.packed);
-            float4* dst4 = reinterpret_cast<float4*>(dst);
-            for (std::uint64_t i = threadIdx.x; i < p.block_floats / 4; i += blockDim.x) dst4[i] = src4[i];
-        } else {
-            for (std::uint64_t i = threadIdx.x; i < p.block_floats; i += blockDim.x) dst[i] = p.packed[i];
+        std::uint64_t* dst = p.words[blockIdx.x] + (static_cast<std::uint64_t>(parity) * p.world + p.rank) * p.block_floats;
+        for (std::uint64_t e = threadIdx.x; e < p.block_floats; e += blockDim.x) {
+            dst[e] = tag | __float_as_uint(p.packed[e]);
         }
-        // Every thread's stores reach the peer before the flag that announces them.
-        __threadfence_system();
-        __syncthreads();
-        if (threadIdx.x == 0) store_release_sys(p.flags[dst_rank] + parity * p.world + p.rank, p.step);
     }
-    // All ranks' blocks of this step in this rank's buffer (bounded waits).
-    const std::uint32_t* own_flags = p.flags[p.rank] + parity * p.world;
+    const std::uint32_t R = p.rows_per_cta;
+    const std::uint64_t r0 = static_cast<std::uint64_t>(blockIdx.x) * R;
+    const std::uint64_t left = r0 < p.rows ? p.rows - r0 : 0;  // rows of this CTA
+    const std::uint32_t nr = static_cast<std::uint32_t>(left < R ? left : R);
+    float* sm_m = parts;
+    float* sm_l = parts + p.world * R;
+    float* sm_o = parts + 2 * p.world * R;
+    const std::uint64_t* own = p.words[p.rank] + static_cast<std::uint64_t>(parity) * p.world * p.block_floats;
+    // Per source rank, this CTA's rows: nr m words, nr l words, nr * D o words.
+    const std::uint32_t per_src = nr * (p.head_dim + 2);
+    // Each thread takes its words eight at a time: the eight loads are in
+    // flight together, and only the words not yet of this step are polled
+    // again.
+    constexpr int kBatch = 8;
+    const std::uint32_t total = p.world * per_src;
+    std::uint32_t budget = kWordPolls;
     bool ok = true;
-    if (threadIdx.x < p.world) {
-        ok = false;
-        for (std::uint32_t poll = 0; poll < kFlagPolls; ++poll) {
-            if (load_acquire_sys(own_flags + threadIdx.x) == p.step) {
-                ok = true;
+    for (std::uint32_t base = threadIdx.x; ok && base < total; base += kBatch * blockDim.x) {
+        const std::uint64_t* w[kBatch];
+        float* slot[kBatch];
+        std::uint64_t v[kBatch];
+        bool need[kBatch];
+#pragma unroll
+        for (int u = 0; u < kBatch; ++u) {
+            const std::uint32_t j = base + u * blockDim.x;
+            need[u] = j < total;
+            w[u] = own;
+            slot[u] = sm_m;
+            if (!need[u]) continue;
+            const std::uint32_t src = j / per_src;
+            const std::uint32_t i = j % per_src;
+            std::uint64_t e;
+            if (i < nr) {
+                e = r0 + i;
+                slot[u] = sm_m + src * R + i;
+            } else if (i < 2 * nr) {
+                e = p.rows + r0 + (i - nr);
+                slot[u] = sm_l + src * R + (i - nr);
+            } else {
+                const std::uint32_t k = i - 2 * nr;
+                e = 2 * p.rows + r0 * p.head_dim + k;  // rows r0.. are contiguous in the o block
+                slot[u] = sm_o + (static_cast<std::uint64_t>(src) * R) * p.head_dim + k;
+            }
+            w[u] = own + static_cast<std::uint64_t>(src) * p.block_floats + e;
+        }
+#pragma unroll
+        for (int u = 0; u < kBatch; ++u) v[u] = need[u] ? load_word(w[u]) : 0;
+        for (;;) {
+            bool waiting = false;
+#pragma unroll
+            for (int u = 0; u < kBatch; ++u) {
+                if (!need[u]) continue;
+                if ((v[u] & 0xFFFFFFFF00000000ull) == tag) {
+                    *slot[u] = __uint_as_float(static_cast<std::uint32_t>(v[u]));
+                    need[u] = false;
+                } else {
+                    waiting = true;
+                }
+            }
+            if (!waiting) break;
+            if (budget == 0) {
+                ok = false;
                 break;
             }
+            --budget;
             __nanosleep(64);
+#pragma unroll
+            for (int u = 0; u < kBatch; ++u) {
+                if (need[u]) v[u] = load_word(w[u]);
+            }
         }
-        if (!ok) flag_error(p.error_word, kErrWaitTimeout);
     }
+    if (!ok) flag_error(p.error_word, kErrWaitTimeout);
     if (!__syncthreads_and(ok)) return;
-    __threadfence();
-    const float* base = p.blocks[p.rank] + static_cast<std::uint64_t>(parity) * p.world * p.block_floats;
     const std::uint32_t warps = blockDim.x / 32;
-    for (std::uint64_t row = static_cast<std::uint64_t>(blockIdx.x) * warps + threadIdx.x / 32; row < p.rows;
-         row += static_cast<std::uint64_t>(gridDim.x) * warps) {
-        lse_merge_row(base, base + p.rows, base + 2 * p.rows, p.world, row, p.head_dim, p.block_floats,
-                      p.block_floats, p.block_floats, p.out, threadIdx.x & 31);
+    for (std::uint32_t k = threadIdx.x / 32; k < nr; k += warps) {
+        lse_merge_row(sm_m, sm_l, sm_o, p.world, k, p.head_dim, R, R,
+                      static_cast<std::uint64_t>(R) * p.head_dim, p.out + r0 * p.head_dim, threadIdx.x & 31);
     }
 }
 
@@ -232,26 +279,25 @@ extern "C" int inferlab_cuda_peer_exchange_combine(InferlabCudaPeerExchange* exc
         std::lock_guard<std::mutex> lock(ex.mutex);
         ilb::DeviceGuard guard(ex.device);
         ilb::ExchangeParams p{};
-        for (std::uint32_t r = 0; r < ex.world; ++r) {
-            auto* base = static_cast<unsigned char*>(ex.bases[r]);
-            p.blocks[r] = reinterpret_cast<float*>(base);
-            p.flags[r] = reinterpret_cast<std::uint32_t*>(base + ex.layout.flags_offset);
-        }
+        for (std::uint32_t r = 0; r < ex.world; ++r) p.words[r] = static_cast<std::uint64_t*>(ex.bases[r]);
         p.packed = packed;
         p.out = out;
         p.rows = ex.rows;
         p.block_floats = ex.layout.block_floats;
+        p.rows_per_cta = static_cast<std::uint32_t>((ex.rows + ex.world - 1) / ex.world);
         p.head_dim = ex.head_dim;
         p.world = ex.world;
         p.rank = ex.rank;
-        // Steps count from 1 (the zeroed flags match no step); a wrap skips 0.
+        // Steps count from 1 (the zeroed words carry step 0); a wrap skips 0.
         if (++ex.step == 0) ex.step = 1;
         p.step = ex.step;
         p.error_word = ex.error_word;
-        if (ex.layout.block_floats % 4 == 0 && reinterpret_cast<std::uintptr_t>(packed) % 16 != 0) {
-            throw std::runtime_error("peer exchange block must be 16-byte aligned");
-        }
-        ilb::peer_exchange_kernel<<<ex.world, ilb::kExchangeThreads, 0, static_cast<cudaStream_t>(stream)>>>(p);
+        const std::size_t smem = static_cast<std::size_t>(ex.world) * p.rows_per_cta * (ex.head_dim + 2) * 4;
+        if (smem > 200 * 1024) throw std::runtime_error("peer exchange rows do not fit a CTA");
+        ilb::cuda_check(cudaFuncSetAttribute(ilb::peer_exchange_kernel,
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)),
+                        "cudaFuncSetAttribute");
+        ilb::peer_exchange_kernel<<<ex.world, ilb::kExchangeThreads, smem, static_cast<cudaStream_t>(stream)>>>(p);
         ilb::cuda_check(cudaGetLastError(), "peer exchange launch");
     });
 }
