@@ -32,9 +32,9 @@ namespace {
 
 constexpr std::uint32_t kMaxRanks = INFERLAB_CUDA_PEER_MAX_RANKS;
 constexpr int kExchangeThreads = 256;
-// Bounded wait for the peers' words: at most 2^25 polls of >= 64 ns per
-// thread (> 2 s), shared by all the words the thread receives.
-constexpr std::uint32_t kWordPolls = 1u << 25;
+// Bounded wait for the peers' words: 2 s of the GPU's global timer per
+// thread, shared by all the words the thread receives.
+constexpr unsigned long long kWaitNs = 2000000000ull;
 
 std::uint64_t align256(std::uint64_t n) { return (n + 255) & ~std::uint64_t(255); }
 
@@ -63,6 +63,12 @@ struct ExchangeParams {
     std::uint32_t step;
     std::uint32_t* error_word;
 };
+
+__device__ __forceinline__ unsigned long long global_ns() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
 
 __device__ __forceinline__ std::uint64_t load_word(const std::uint64_t* p) {
     std::uint64_t v;
@@ -98,7 +104,7 @@ __global__ void __launch_bounds__(kExchangeThreads) peer_exchange_kernel(const E
     // again.
     constexpr int kBatch = 8;
     const std::uint32_t total = p.world * per_src;
-    std::uint32_t budget = kWordPolls;
+    const unsigned long long deadline = global_ns() + kWaitNs;
     bool ok = true;
     for (std::uint32_t base = threadIdx.x; ok && base < total; base += kBatch * blockDim.x) {
         const std::uint64_t* w[kBatch];
@@ -143,11 +149,10 @@ __global__ void __launch_bounds__(kExchangeThreads) peer_exchange_kernel(const E
                 }
             }
             if (!waiting) break;
-            if (budget == 0) {
+            if (global_ns() > deadline) {
                 ok = false;
                 break;
             }
-            --budget;
             __nanosleep(64);
 #pragma unroll
             for (int u = 0; u < kBatch; ++u) {

@@ -77,3 +77,55 @@ def test_split_sequence_over_nccl_matches_single_gpu(tmp_path, world):
     assert np.all(err <= 1e-6 + 1e-5 * np.abs(whole)), float(err.max())
     for x in peer:
         assert np.array_equal(x, merged)
+
+
+def _missing_peer_main(rank, world, port, path):
+    import torch
+    import torch.distributed as dist
+
+    from inferlab_b200 import AttentionError, distributed
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=60),
+                            device_id=torch.device(f"cuda:{rank}"))
+    try:
+        exchange = distributed.PeerExchange(4, 64)
+        block = torch.zeros(4 * 66, dtype=torch.float32, device=f"cuda:{rank}")
+        block[4:8] = 1.0  # l = 1 for every row, m = 0, o = 0
+        outcome = "no error"
+        if rank == 0:
+            # rank 1 leaves this step out (between steps, nothing of its own in
+            # flight): rank 0's bounded wait runs out and reports it
+            exchange.combine(block)
+            try:
+                exchange.synchronize(timeout_ms=30000)
+            except AttentionError as caught:
+                outcome = str(caught)
+            with open(path, "w") as f:
+                f.write(outcome)
+        dist.barrier()
+        exchange.close()
+    finally:
+        dist.destroy_process_group()
+
+
+def test_peer_exchange_reports_a_missing_peer(tmp_path):
+    """Failure detection without a GPU fault: one rank skips an exchange, the
+    other's bounded wait (about 2 s) gives up and its synchronize raises
+    "device wait timed out"; the CUDA context stays usable and both ranks
+    close cleanly. NVLS stays off (NCCL_NVLS_ENABLE=0); the exchange itself
+    uses plain peer stores."""
+    import torch
+    import torch.multiprocessing as mp
+
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    path = str(tmp_path / "outcome.txt")
+    mp.start_processes(_missing_peer_main, args=(2, _port(), path), nprocs=2,
+                       start_method="spawn", join=True)
+    with open(path) as f:
+        assert f.read() == "device wait timed out"
