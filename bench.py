@@ -695,11 +695,11 @@ def measure_prefill(args, dist, world, rank, device, peaks, peak_kind):
 # one long sequence split across the ranks
 # ---------------------------------------------------------------------------
 def measure_long_sequence(args, dist, world, rank, device, peaks, peak_kind):
-    """One 131072-token sequence split across the ranks: per step, decode
-    partials over the local blocks into one packed [m | l | o] block, then (at
-    N > 1) one kernel that stores the block into every peer's receive buffer
-    over NVLink, waits for all ranks' blocks and merges them in rank order
-    (distributed.PeerExchange). The NCCL all-gather + merge of the same
+    """One 131072-token sequence split across the ranks: per step (at N > 1)
+    ONE kernel decodes the local blocks, and the CTA that finishes each
+    kv-head stores its rows' (m, l, o) into every peer's receive buffer over
+    NVLink, waits for those rows from all ranks and merges them in rank order
+    (distributed.PeerExchange.decode). The NCCL all-gather + merge of the same
     partials is timed beside it. Timed per rank with events, max over ranks."""
     import torch
 
@@ -762,12 +762,13 @@ def measure_long_sequence(args, dist, world, rank, device, peaks, peak_kind):
         "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded)",
         "config": {"workload": "one 131072-token sequence, GQA 32/8 x 128 bf16, blocks split "
                                "across GPUs, (m, l, o) partials exchanged and merged in rank order"
-                               + (" in one kernel over NVLink peer memory" if exchange is not None
-                                  else ""),
+                               + (", decode and exchange in one kernel over NVLink peer memory"
+                                  if exchange is not None else ""),
                    "tokens_this_rank": local, "comm_nranks": comm,
-                   "collective": ("peer stores over NVLink inside the merge kernel "
-                                  "(inferlab_cuda_peer_exchange_combine), "
-                                  f"{32 * 130 * 4} B from every rank to every peer, flags per step"
+                   "collective": ("peer stores over NVLink inside the decode kernel "
+                                  "(inferlab_cuda_paged_decode_exchange): each kv-head's rows "
+                                  "of (m, l, o) from every rank to every peer as step-tagged "
+                                  "8-byte words"
                                   if exchange is not None else
                                   f"all_gather_into_tensor over NCCL ({exchange_error})"
                                   if comm and comm > 1 else "none (one GPU)"),
@@ -776,7 +777,7 @@ def measure_long_sequence(args, dist, world, rank, device, peaks, peak_kind):
                      "peak": peaks["hbm_gbs"], "unit": "GB/s",
                      "frac": round(value / world / peaks["hbm_gbs"], 4),
                      "peak_kind": f"{peak_kind} hbm_gbs"},
-        "gpu_launches": 2 * args.steps, "clocks": clock,
+        "gpu_launches": (1 if exchange is not None else 2) * args.steps, "clocks": clock,
         "per_rank": per_rank(dist, ms_per_step=ms / args.steps, sm_mhz=clock["sm_mhz"]),
     }
     if nccl is not None:

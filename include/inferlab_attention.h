@@ -550,6 +550,26 @@ int inferlab_cuda_peer_exchange_synchronize(InferlabCudaPeerExchange* exchange, 
 /* Closes the peers' buffers; every rank must have finished its exchanges. */
 void inferlab_cuda_peer_exchange_destroy(InferlabCudaPeerExchange* exchange);
 
+/*
+ * The split-sequence decode and the exchange in ONE kernel: this rank decodes
+ * its block range (the inferlab_cuda_paged_decode_partials arguments), and
+ * the CTA that finishes each (sequence, kv-head) stores that kv-head's rows of
+ * (m, l, o) into every rank's receive buffer of `exchange` (created with rows
+ * = num_seqs * q_heads and the pool's head_dim), waits (bounded) for those
+ * rows from all ranks and merges them in rank order into out [num_seqs *
+ * q_heads][head_dim] - the same bits as partials + exchange_combine. Takes
+ * one step of `exchange`, like inferlab_cuda_peer_exchange_combine; a rank
+ * with no blocks of the sequence calls that instead with an empty block.
+ * Needs the fast decode kernel's pool geometry, and at most half of the
+ * GPU's resident decode CTAs may wait at once (num_seqs * kv_heads).
+ */
+int inferlab_cuda_paged_decode_exchange(InferlabCudaKvPool* pool, const float* queries,
+                                        const int32_t* block_tables, uint32_t max_blocks,
+                                        const int32_t* context_lens, uint32_t num_seqs,
+                                        uint32_t q_heads, uint32_t max_context_len, void* workspace,
+                                        size_t workspace_bytes, InferlabCudaPeerExchange* exchange,
+                                        float* out, void* stream, char* error, size_t error_capacity);
+
 /* Library version string, e.g. "inferlab-b200 0.1 sm_100a". */
 const char* inferlab_cuda_version(void);
 

@@ -102,6 +102,9 @@ SIGNATURES = {
     "inferlab_cuda_peer_exchange_synchronize": (ctypes.c_int, [
         c_vp, c_vp, ctypes.c_uint32, c_err, c_sz]),
     "inferlab_cuda_peer_exchange_destroy": (None, [c_vp]),
+    "inferlab_cuda_paged_decode_exchange": (ctypes.c_int, [
+        c_vp, c_vp, c_vp, ctypes.c_uint32, c_vp, ctypes.c_uint32, ctypes.c_uint32,
+        ctypes.c_uint32, c_vp, c_sz, c_vp, c_vp, c_vp, c_err, c_sz]),
     "inferlab_cuda_pool_info": (ctypes.c_int, [
         c_vp, ctypes.POINTER(InferlabCudaPoolInfo), c_err, c_sz]),
     "inferlab_cuda_pool_synchronize": (ctypes.c_int, [c_vp, c_vp, ctypes.c_uint32, c_err, c_sz]),

@@ -4,6 +4,8 @@
 
 #include "pool.cuh"
 
+struct InferlabCudaPeerExchange;
+
 namespace ilb {
 
 // Bytes of decode workspace a batch of this shape needs, and how many of its
@@ -30,6 +32,23 @@ void launch_paged_decode(InferlabCudaKvPool& pool, const float* queries,
                          const std::int32_t* context_lens, std::uint32_t num_seqs,
                          std::uint32_t q_heads, std::uint32_t max_context_len, float* out,
                          void* workspace, std::size_t workspace_bytes, cudaStream_t stream);
+
+// The buffers of a peer exchange (peer_exchange.cu) for one call: every
+// rank's receive words, this rank, the exchanged block's rows and head_dim,
+// and the call's step number (taken by exchange_take_step).
+struct ExchangeView {
+    std::uint64_t* words[8];
+    std::uint32_t world;
+    std::uint32_t rank;
+    std::uint32_t step;
+    std::uint64_t rows;
+    std::uint32_t head_dim;
+    int device;
+};
+
+// Takes the next step of `exchange` (serialised per exchange) and describes
+// its buffers; throws on a null exchange.
+ExchangeView exchange_take_step(InferlabCudaPeerExchange* exchange);
 
 // Launches kv_append (see inferlab_cuda_kv_append); the pool's device must be
 // current.

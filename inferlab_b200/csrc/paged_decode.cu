@@ -102,6 +102,16 @@ struct DecodeParams {
     float* ws_ml;            // [seq][q_head][split][2]
     std::uint32_t* ws_count; // [seq][kv_head]
     std::uint32_t* error_word;
+    // Split-sequence decode with the peer exchange fused (kExchange kernels
+    // only): the CTA that finishes a (sequence, kv-head) stores its rows'
+    // (m, l, o) as step-tagged words into every rank's receive buffer, waits
+    // for those rows from all ranks and merges them into xout.
+    std::uint64_t* xwords[8];
+    float* xout;
+    std::uint64_t xrows;  // rows of the exchanged block: num_seqs * q_heads
+    std::uint32_t xworld;
+    std::uint32_t xrank;
+    std::uint32_t xstep;
 };
 
 // Shared-memory layout of one CTA.
@@ -160,9 +170,116 @@ __device__ __forceinline__ void widen16_pairs(const uint4& raw, std::uint64_t* o
     for (int i = 0; i < 4; ++i) out[i] = pack_u32x2(w[i] << 16, w[i] & 0xFFFF0000u);
 }
 
-template <typename KvT, int D, int GROUP>
+// Fused split-sequence exchange: word index of element (row, dim) in the
+// packed [m | l | o] block, and the step-tagged store of one element into
+// slot `xrank` of every rank's receive buffer (plain peer stores through
+// NVSwitch, no multicast; an aligned 8-byte store is single-copy atomic, so a
+// receiver that sees the step also sees the value).
+template <int D>
+__device__ __forceinline__ void push_word(const DecodeParams& p, std::uint64_t index, float value) {
+    const std::uint64_t block = p.xrows * (D + 2);
+    const std::uint64_t word = (static_cast<std::uint64_t>(p.xstep) << 32) | __float_as_uint(value);
+    const std::uint64_t at = (static_cast<std::uint64_t>(p.xstep & 1u) * p.xworld + p.xrank) * block + index;
+    for (std::uint32_t r = 0; r < p.xworld; ++r) p.xwords[r][at] = word;
+}
+
+__device__ __forceinline__ unsigned long long global_ns() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+__device__ __forceinline__ std::uint64_t load_word(const std::uint64_t* w) {
+    std::uint64_t v;
+    asm volatile("ld.volatile.global.u64 %0, [%1];" : "=l"(v) : "l"(w) : "memory");
+    return v;
+}
+
+// The CTA that finished rows [row0, row0 + GROUP) has pushed them; it now
+// receives those rows of every rank's block (bounded: 2 s of the global
+// timer, a timeout records kErrWaitTimeout), stages them in `stage` (shared
+// memory, world x GROUP x (D + 2) floats) and merges them in rank order into
+// xout with the same per-row code as the standalone combine.
+template <int D, int GROUP>
+__device__ void receive_and_merge(const DecodeParams& p, std::size_t row0, float* stage) {
+    const std::uint64_t block = p.xrows * (D + 2);
+    const std::uint64_t tag = static_cast<std::uint64_t>(p.xstep) << 32;
+    const std::uint64_t* own = p.xwords[p.xrank] + static_cast<std::uint64_t>(p.xstep & 1u) * p.xworld * block;
+    float* sm_m = stage;
+    float* sm_l = stage + p.xworld * GROUP;
+    float* sm_o = stage + 2 * p.xworld * GROUP;
+    constexpr std::uint32_t kPerSrc = GROUP * (D + 2);
+    const std::uint32_t total = p.xworld * kPerSrc;
+    const unsigned long long deadline = global_ns() + 2000000000ull;
+    bool ok = true;
+    constexpr int kBatch = 8;
+    for (std::uint32_t base = threadIdx.x; ok && base < total; base += kBatch * blockDim.x) {
+        const std::uint64_t* w[kBatch];
+        float* slot[kBatch];
+        std::uint64_t v[kBatch];
+        bool need[kBatch];
+#pragma unroll
+        for (int u = 0; u < kBatch; ++u) {
+            const std::uint32_t j = base + u * blockDim.x;
+            need[u] = j < total;
+            w[u] = own;
+            slot[u] = sm_m;
+            if (!need[u]) continue;
+            const std::uint32_t src = j / kPerSrc;
+            const std::uint32_t i = j % kPerSrc;
+            std::uint64_t e;
+            if (i < GROUP) {
+                e = row0 + i;
+                slot[u] = sm_m + src * GROUP + i;
+            } else if (i < 2 * GROUP) {
+                e = p.xrows + row0 + (i - GROUP);
+                slot[u] = sm_l + src * GROUP + (i - GROUP);
+            } else {
+                const std::uint32_t k = i - 2 * GROUP;
+                e = 2 * p.xrows + row0 * D + k;
+                slot[u] = sm_o + src * (GROUP * D) + k;
+            }
+            w[u] = own + src * block + e;
+        }
+#pragma unroll
+        for (int u = 0; u < kBatch; ++u) v[u] = need[u] ? load_word(w[u]) : 0;
+        for (;;) {
+            bool waiting = false;
+#pragma unroll
+            for (int u = 0; u < kBatch; ++u) {
+                if (!need[u]) continue;
+                if ((v[u] & 0xFFFFFFFF00000000ull) == tag) {
+                    *slot[u] = __uint_as_float(static_cast<std::uint32_t>(v[u]));
+                    need[u] = false;
+                } else {
+                    waiting = true;
+                }
+            }
+            if (!waiting) break;
+            if (global_ns() > deadline) {
+                ok = false;
+                break;
+            }
+            __nanosleep(64);
+#pragma unroll
+            for (int u = 0; u < kBatch; ++u) {
+                if (need[u]) v[u] = load_word(w[u]);
+            }
+        }
+    }
+    if (!ok) flag_error(p.error_word, kErrWaitTimeout);
+    if (!__syncthreads_and(ok)) return;
+    for (int h = threadIdx.x / 32; h < GROUP; h += blockDim.x / 32) {
+        lse_merge_row(sm_m, sm_l, sm_o, p.xworld, h, D, GROUP, GROUP, GROUP * D, p.xout + row0 * D,
+                      threadIdx.x & 31);
+    }
+}
+
+template <typename KvT, int D, int GROUP, bool kExchange = false>
 // Three CTAs per SM for groups of up to four q-heads (the fp32 pairs of q and
 // the accumulators fit ~168 registers); GQA-8 keeps the compiler's choice.
+// kExchange: the split-sequence variant, whose CTAs that finish a (sequence,
+// kv-head) exchange its rows with the other ranks and merge them.
 __global__ void __launch_bounds__(kDecodeWarps * 32, GROUP >= 8 ? 1 : 3)
     paged_decode_kernel(const DecodeParams p) {
     using S = DecodeShape<KvT, D, GROUP>;
@@ -558,7 +675,13 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, GROUP >= 8 ? 1 : 3)
         }
         const std::size_t row = row0 + h;
         if (single) {
-            if (p.emit_partials) {
+            if constexpr (kExchange) {
+                push_word<D>(p, 2 * p.xrows + row * D + dim, a);
+                if (dim == 0) {
+                    push_word<D>(p, row, mw * kLn2);
+                    push_word<D>(p, p.xrows + row, lsum);
+                }
+            } else if (p.emit_partials) {
                 p.part_o[row * D + dim] = a;
                 if (dim == 0) {
                     p.part_m[row] = mw * kLn2;
@@ -577,7 +700,13 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, GROUP >= 8 ? 1 : 3)
             }
         }
     }
-    if (single) return;
+    if (single) {
+        if constexpr (kExchange) {
+            __syncthreads();  // the tile area is free: it stages the received rows
+            receive_and_merge<D, GROUP>(p, row0, reinterpret_cast<float*>(smem));
+        }
+        return;
+    }
 
     // Fused split combine: the last CTA of this (sequence, kv-head) merges.
     __threadfence();
@@ -645,7 +774,16 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, GROUP >= 8 ? 1 : 3)
         }
         const float mw = red_ml(0, h)[0];
         const float lsum = red_ml(0, h)[1];
-        if (p.emit_partials) {
+        if constexpr (kExchange) {
+            push_word<D>(p, 2 * p.xrows + row * D + dim, a.x);
+            push_word<D>(p, 2 * p.xrows + row * D + dim + 1, a.y);
+            push_word<D>(p, 2 * p.xrows + row * D + dim + 2, a.z);
+            push_word<D>(p, 2 * p.xrows + row * D + dim + 3, a.w);
+            if (dim == 0) {
+                push_word<D>(p, row, mw * kLn2);
+                push_word<D>(p, p.xrows + row, lsum);
+            }
+        } else if (p.emit_partials) {
             *reinterpret_cast<float4*>(p.part_o + row * D + dim) = a;
             if (dim == 0) {
                 p.part_m[row] = mw * kLn2;
@@ -658,6 +796,10 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, GROUP >= 8 ? 1 : 3)
         }
     }
     if (threadIdx.x == 0) p.ws_count[pair] = 0;
+    if constexpr (kExchange) {
+        __syncthreads();  // the split weights in the tile area are dead
+        receive_and_merge<D, GROUP>(p, row0, reinterpret_cast<float*>(smem));
+    }
 }
 
 // K4: log-sum-exp merge of partials in part order; one warp per row.
@@ -724,13 +866,13 @@ std::size_t workspace_bytes_for(std::uint32_t num_seqs, std::uint32_t q_heads,
 
 using DecodeKernel = void (*)(const DecodeParams);
 
-template <typename KvT, int D>
+template <typename KvT, int D, bool kExchange = false>
 DecodeKernel pick_group(std::uint32_t group) {
     switch (group) {
-        case 1: return paged_decode_kernel<KvT, D, 1>;
-        case 2: return paged_decode_kernel<KvT, D, 2>;
-        case 4: return paged_decode_kernel<KvT, D, 4>;
-        case 8: return paged_decode_kernel<KvT, D, 8>;
+        case 1: return paged_decode_kernel<KvT, D, 1, kExchange>;
+        case 2: return paged_decode_kernel<KvT, D, 2, kExchange>;
+        case 4: return paged_decode_kernel<KvT, D, 4, kExchange>;
+        case 8: return paged_decode_kernel<KvT, D, 8, kExchange>;
         default: return nullptr;
     }
 }
@@ -746,26 +888,35 @@ std::size_t smem_for_group(std::uint32_t group) {
     }
 }
 
-template <typename KvT>
+template <typename KvT, bool kExchange = false>
 DecodeKernel pick_kernel(std::uint32_t head_dim, std::uint32_t group, std::size_t& smem) {
     if (head_dim == 64) {
         smem = smem_for_group<KvT, 64>(group);
-        return pick_group<KvT, 64>(group);
+        return pick_group<KvT, 64, kExchange>(group);
     }
     if (head_dim == 128) {
         smem = smem_for_group<KvT, 128>(group);
-        return pick_group<KvT, 128>(group);
+        return pick_group<KvT, 128, kExchange>(group);
     }
     return nullptr;
 }
 
 // The fast kernel covers block_tokens 16, head_dim 64/128 and GQA groups of
 // 1/2/4/8; other pool geometries use the generic CUDA-core kernel.
-DecodeKernel select_decode(const InferlabCudaKvPool& pool, std::uint32_t group, std::size_t& smem) {
+// `exchange` picks the split-sequence variant with the peer exchange fused.
+DecodeKernel select_decode(const InferlabCudaKvPool& pool, std::uint32_t group, std::size_t& smem,
+                           bool exchange = false) {
     if (pool.block_tokens != kDecodeBlockTokens) return nullptr;
-    if (pool.dtype == kFp32) return pick_kernel<float>(pool.head_dim, group, smem);
-    if (pool.dtype == kF16) return pick_kernel<__half>(pool.head_dim, group, smem);
-    return pick_kernel<__nv_bfloat16>(pool.head_dim, group, smem);
+    if (pool.dtype == kFp32) {
+        return exchange ? pick_kernel<float, true>(pool.head_dim, group, smem)
+                        : pick_kernel<float>(pool.head_dim, group, smem);
+    }
+    if (pool.dtype == kF16) {
+        return exchange ? pick_kernel<__half, true>(pool.head_dim, group, smem)
+                        : pick_kernel<__half>(pool.head_dim, group, smem);
+    }
+    return exchange ? pick_kernel<__nv_bfloat16, true>(pool.head_dim, group, smem)
+                    : pick_kernel<__nv_bfloat16>(pool.head_dim, group, smem);
 }
 
 // CTAs of `kernel` resident per SM times the SMs of `device` (cached per
@@ -836,12 +987,16 @@ void run_decode(InferlabCudaKvPool& p, const float* queries, const std::int32_t*
                 std::uint32_t max_blocks, const std::int32_t* context_lens, std::uint32_t num_seqs,
                 std::uint32_t q_heads, std::uint32_t max_context_len, float* out, float* part_m,
                 float* part_l, float* part_o, void* workspace, std::size_t workspace_bytes,
-                cudaStream_t stream) {
+                cudaStream_t stream, const ExchangeView* xview = nullptr) {
     const std::uint32_t group = q_heads / p.kv_heads;
     std::size_t smem = 0;
-    DecodeKernel kernel = select_decode(p, group, smem);
+    DecodeKernel kernel = select_decode(p, group, smem, xview != nullptr);
     if (kernel == nullptr) {
         // Generic CUDA-core path (any head_dim / block size / group).
+        if (xview != nullptr) {
+            throw std::runtime_error(
+                "paged decode exchange needs block_tokens 16, head_dim 64 or 128 and a GQA group of 1, 2, 4 or 8");
+        }
         if (part_m != nullptr) {
             throw std::runtime_error(
                 "paged decode partials need block_tokens 16, head_dim 64 or 128 and a GQA group of 1, 2, 4 or 8");
@@ -932,6 +1087,14 @@ void run_decode(InferlabCudaKvPool& p, const float* queries, const std::int32_t*
         d.ws_o = reinterpret_cast<float*>(base + counters + ml);
     }
     d.error_word = p.error_word;
+    if (xview != nullptr) {
+        for (std::uint32_t r = 0; r < xview->world; ++r) d.xwords[r] = xview->words[r];
+        d.xout = out;
+        d.xrows = xview->rows;
+        d.xworld = xview->world;
+        d.xrank = xview->rank;
+        d.xstep = xview->step;
+    }
     cuda_check(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                     static_cast<int>(smem)),
                "cudaFuncSetAttribute");
@@ -984,6 +1147,44 @@ void launch_paged_decode(InferlabCudaKvPool& pool, const float* queries,
 }
 
 }  // namespace ilb
+
+extern "C" int inferlab_cuda_paged_decode_exchange(InferlabCudaKvPool* pool, const float* queries,
+                                                   const std::int32_t* block_tables, std::uint32_t max_blocks,
+                                                   const std::int32_t* context_lens, std::uint32_t num_seqs,
+                                                   std::uint32_t q_heads, std::uint32_t max_context_len,
+                                                   void* workspace, std::size_t workspace_bytes,
+                                                   InferlabCudaPeerExchange* exchange, float* out, void* stream,
+                                                   char* error, std::size_t error_capacity) {
+    return ilb::protect(error, error_capacity, [&] {
+        auto& p = ilb::checked_pool(pool);
+        ilb::validate_decode(p, queries, block_tables, max_blocks, context_lens, num_seqs, q_heads,
+                             max_context_len);
+        if (out == nullptr) throw std::runtime_error("paged decode pointer is null");
+        if (num_seqs == 0) return;
+        std::size_t smem = 0;
+        ilb::DecodeKernel kernel = ilb::select_decode(p, q_heads / p.kv_heads, smem);
+        if (kernel == nullptr) {
+            throw std::runtime_error(
+                "paged decode exchange needs block_tokens 16, head_dim 64 or 128 and a GQA group of 1, 2, 4 or 8");
+        }
+        // The CTAs that finish a (sequence, kv-head) wait for the other ranks'
+        // matching CTAs; they must never fill the GPU, or a rank could hold
+        // every slot waiting while the CTAs its peers wait for are unscheduled.
+        const std::uint32_t slots = ilb::resident_slots(kernel, smem, p.device);
+        if (slots == 0 || static_cast<std::uint64_t>(num_seqs) * p.kv_heads * 2 > slots) {
+            throw std::runtime_error("paged decode exchange batch is too large for one launch");
+        }
+        ilb::DeviceGuard guard(p.device);
+        const ilb::ExchangeView view = ilb::exchange_take_step(exchange);
+        if (view.device != p.device || view.rows != static_cast<std::uint64_t>(num_seqs) * q_heads ||
+            view.head_dim != p.head_dim) {
+            throw std::runtime_error("peer exchange does not match the decode batch");
+        }
+        ilb::run_decode(p, queries, block_tables, max_blocks, context_lens, num_seqs, q_heads,
+                        max_context_len, out, nullptr, nullptr, nullptr, workspace, workspace_bytes,
+                        static_cast<cudaStream_t>(stream), &view);
+    });
+}
 
 extern "C" std::size_t inferlab_cuda_paged_decode_workspace_size(const InferlabCudaKvPool* pool,
                                                                  std::uint32_t num_seqs,

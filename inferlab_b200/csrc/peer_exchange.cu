@@ -20,6 +20,7 @@
 // only after its own exchange s + 1 has read that peer's step s + 1 words,
 // which the peer wrote only after its exchange s had read its step s words.
 #include "common.cuh"
+#include "internal.cuh"
 #include "lse_merge.cuh"
 
 #include "../../include/inferlab_attention.h"
@@ -184,6 +185,26 @@ struct InferlabCudaPeerExchange {
     std::uint32_t step = 0;
     std::mutex mutex;
 };
+
+namespace ilb {
+
+ExchangeView exchange_take_step(InferlabCudaPeerExchange* exchange) {
+    if (exchange == nullptr) throw std::runtime_error("peer exchange pointer is null");
+    auto& ex = *exchange;
+    std::lock_guard<std::mutex> lock(ex.mutex);
+    ExchangeView v{};
+    for (std::uint32_t r = 0; r < ex.world; ++r) v.words[r] = static_cast<std::uint64_t*>(ex.bases[r]);
+    v.world = ex.world;
+    v.rank = ex.rank;
+    if (++ex.step == 0) ex.step = 1;  // the zeroed words carry step 0
+    v.step = ex.step;
+    v.rows = ex.rows;
+    v.head_dim = ex.head_dim;
+    v.device = ex.device;
+    return v;
+}
+
+}  // namespace ilb
 
 extern "C" std::uint64_t inferlab_cuda_peer_buffer_bytes(std::uint32_t world, std::uint64_t rows,
                                                          std::uint32_t head_dim) {

@@ -152,6 +152,27 @@ class PeerExchange:
             len(error)), error)
         return out
 
+    def decode(self, pool, queries, block_table, context_lens, max_context_len: int, workspace=None,
+               out=None, stream=None):
+        """This rank's block range decoded and exchanged in one kernel
+        (inferlab_cuda_paged_decode_exchange): the merged [rows, q_heads,
+        head_dim] output of all ranks' ranges, asynchronous."""
+        import torch
+
+        from . import _lib
+        from .paged import _check, _stream_handle, _vp
+
+        num_seqs, q_heads, hd = queries.shape
+        if out is None:
+            out = torch.empty((num_seqs, q_heads, hd), dtype=torch.float32, device=queries.device)
+        ws_bytes = 0 if workspace is None else workspace.numel() * workspace.element_size()
+        error = _lib.error_buffer()
+        _check(self._lib.inferlab_cuda_paged_decode_exchange(
+            pool._handle, _vp(queries), _vp(block_table), block_table.shape[1], _vp(context_lens),
+            num_seqs, q_heads, int(max_context_len), _vp(workspace), ws_bytes, self._handle,
+            _vp(out), _stream_handle(self.device, stream), error, len(error)), error)
+        return out
+
     def synchronize(self, stream=None, timeout_ms: int = 0) -> None:
         """Waits for the stream and raises if a peer's block never arrived."""
         from . import _lib
@@ -192,10 +213,11 @@ def decode_split_sequence(pool, queries, block_table, local_len: int, group=None
     [rows, blocks]) covering `local_len` tokens. Returns the merged output
     [rows, q_heads, head_dim] on every rank.
 
-    The partials are written straight into one packed [m | l | o] block; with
-    `exchange` one kernel pushes it to every peer over NVLink and merges all
-    ranks' blocks in rank order, otherwise the blocks of all ranks are
-    exchanged with a single all-gather (NCCL) and one kernel merges them."""
+    With `exchange`, one kernel decodes this rank's range and exchanges and
+    merges the partials of all ranks over NVLink (a rank without blocks
+    exchanges an empty block). Otherwise the partials are written straight
+    into one packed [m | l | o] block, the blocks of all ranks are exchanged
+    with a single all-gather (NCCL), and one kernel merges them."""
     import torch
     import torch.distributed as dist
 
@@ -204,6 +226,15 @@ def decode_split_sequence(pool, queries, block_table, local_len: int, group=None
     rows, q_heads, hd = queries.shape
     nrows = rows * q_heads
     world = dist.get_world_size(group) if dist.is_initialized() else 1
+    if exchange is not None and local_len > 0:
+        key = (queries.device.index, rows, local_len)
+        lens = _LENGTHS.get(key)
+        if lens is None:
+            lens = _LENGTHS[key] = torch.full((rows,), local_len, dtype=torch.int32,
+                                              device=queries.device)
+        if workspace is None:
+            workspace = pool.make_workspace(rows, q_heads, local_len)
+        return exchange.decode(pool, queries, block_table, lens, local_len, workspace=workspace)
     send = torch.empty(nrows * (hd + 2), dtype=torch.float32, device=queries.device)
     if local_len > 0:
         key = (queries.device.index, rows, local_len)

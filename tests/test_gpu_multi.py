@@ -4,10 +4,11 @@ One 131,072-token sequence (GQA 32/8 x 128, bf16) split across the GPUs by
 contiguous block ranges: each rank decodes its range into (m, l, o)
 partials, the partials are all-gathered over NCCL and merged in rank order;
 the result must equal the whole-context decode on one GPU within the fp32
-tolerance |a - b| <= 1e-6 + 1e-5 |b|. The same partials exchanged and merged
-in one kernel over NVLink peer memory (distributed.PeerExchange, five calls
-in a row so both buffer parities are reused) must equal the NCCL result bit
-for bit. Ranks are spawned processes with a short process-group timeout.
+tolerance |a - b| <= 1e-6 + 1e-5 |b|. The decode with the exchange fused
+into it over NVLink peer memory (distributed.PeerExchange, five steps in a
+row so both buffer parities are reused), and then the packed partials
+through the standalone exchange kernel, must equal the NCCL result bit for
+bit. Ranks are spawned processes with a short process-group timeout.
 """
 import datetime
 import os
@@ -47,8 +48,15 @@ def _rank_main(rank, world, port, path):
         blocks = full.block_tables[:, lo // 16:(hi + 15) // 16].contiguous()
         merged = distributed.decode_split_sequence(full.pool, full.queries, blocks, hi - lo)
         exchange = distributed.PeerExchange(32, 128)
+        # the decode and the exchange in one kernel, five steps in a row
         peer = [distributed.decode_split_sequence(full.pool, full.queries, blocks, hi - lo,
                                                   exchange=exchange).clone() for _ in range(5)]
+        # then the packed partials through the standalone exchange kernel
+        send = torch.empty(32 * 130, dtype=torch.float32, device=f"cuda:{rank}")
+        lens = torch.full((1,), hi - lo, dtype=torch.int32, device=f"cuda:{rank}")
+        for _ in range(2):
+            full.pool.decode_partials(full.queries, blocks, lens, hi - lo, packed=send)
+            peer.append(exchange.combine(send).view(1, 32, 128).clone())
         exchange.synchronize(timeout_ms=20000)
         exchange.close()
         whole = full.pool.decode(full.queries, full.block_tables, full.context_lens, total)
