@@ -47,8 +47,10 @@ struct ExchangeView {
 };
 
 // Takes the next step of `exchange` (serialised per exchange) and describes
-// its buffers; throws on a null exchange.
-ExchangeView exchange_take_step(InferlabCudaPeerExchange* exchange);
+// its buffers; throws, without taking a step, on a null exchange or one made
+// for another device, row count or head_dim.
+ExchangeView exchange_take_step(InferlabCudaPeerExchange* exchange, int device, std::uint64_t rows,
+                                std::uint32_t head_dim);
 
 // Launches kv_append (see inferlab_cuda_kv_append); the pool's device must be
 // current.

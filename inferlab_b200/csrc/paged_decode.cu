@@ -1161,8 +1161,9 @@ extern "C" int inferlab_cuda_paged_decode_exchange(InferlabCudaKvPool* pool, con
                              max_context_len);
         if (out == nullptr) throw std::runtime_error("paged decode pointer is null");
         if (num_seqs == 0) return;
+        ilb::DeviceGuard guard(p.device);
         std::size_t smem = 0;
-        ilb::DecodeKernel kernel = ilb::select_decode(p, q_heads / p.kv_heads, smem);
+        ilb::DecodeKernel kernel = ilb::select_decode(p, q_heads / p.kv_heads, smem, true);
         if (kernel == nullptr) {
             throw std::runtime_error(
                 "paged decode exchange needs block_tokens 16, head_dim 64 or 128 and a GQA group of 1, 2, 4 or 8");
@@ -1174,12 +1175,20 @@ extern "C" int inferlab_cuda_paged_decode_exchange(InferlabCudaKvPool* pool, con
         if (slots == 0 || static_cast<std::uint64_t>(num_seqs) * p.kv_heads * 2 > slots) {
             throw std::runtime_error("paged decode exchange batch is too large for one launch");
         }
-        ilb::DeviceGuard guard(p.device);
-        const ilb::ExchangeView view = ilb::exchange_take_step(exchange);
-        if (view.device != p.device || view.rows != static_cast<std::uint64_t>(num_seqs) * q_heads ||
-            view.head_dim != p.head_dim) {
-            throw std::runtime_error("peer exchange does not match the decode batch");
+        // Every check that can reject the call runs before the step is taken:
+        // a rank whose call failed after taking it would wait one step ahead
+        // of its peers from then on.
+        if (reinterpret_cast<std::uintptr_t>(queries) % 16 != 0) {
+            throw std::runtime_error("paged decode queries must be 16-byte aligned");
         }
+        const ilb::DecodePlan plan = ilb::full_plan(p, num_seqs, q_heads, max_context_len);
+        const std::size_t need =
+            ilb::workspace_bytes_for(num_seqs, q_heads, p.kv_heads, p.head_dim, plan);
+        if (plan.max_splits > 1 && (workspace == nullptr || workspace_bytes < need)) {
+            throw std::runtime_error("paged decode workspace is too small");
+        }
+        const ilb::ExchangeView view = ilb::exchange_take_step(
+            exchange, p.device, static_cast<std::uint64_t>(num_seqs) * q_heads, p.head_dim);
         ilb::run_decode(p, queries, block_tables, max_blocks, context_lens, num_seqs, q_heads,
                         max_context_len, out, nullptr, nullptr, nullptr, workspace, workspace_bytes,
                         static_cast<cudaStream_t>(stream), &view);

@@ -188,10 +188,14 @@ struct InferlabCudaPeerExchange {
 
 namespace ilb {
 
-ExchangeView exchange_take_step(InferlabCudaPeerExchange* exchange) {
+ExchangeView exchange_take_step(InferlabCudaPeerExchange* exchange, int device, std::uint64_t rows,
+                                std::uint32_t head_dim) {
     if (exchange == nullptr) throw std::runtime_error("peer exchange pointer is null");
     auto& ex = *exchange;
     std::lock_guard<std::mutex> lock(ex.mutex);
+    if (ex.device != device || ex.rows != rows || ex.head_dim != head_dim) {
+        throw std::runtime_error("peer exchange does not match the decode batch");
+    }
     ExchangeView v{};
     for (std::uint32_t r = 0; r < ex.world; ++r) v.words[r] = static_cast<std::uint64_t*>(ex.bases[r]);
     v.world = ex.world;
@@ -314,12 +318,14 @@ extern "C" int inferlab_cuda_peer_exchange_combine(InferlabCudaPeerExchange* exc
         p.head_dim = ex.head_dim;
         p.world = ex.world;
         p.rank = ex.rank;
-        // Steps count from 1 (the zeroed words carry step 0); a wrap skips 0.
-        if (++ex.step == 0) ex.step = 1;
-        p.step = ex.step;
         p.error_word = ex.error_word;
         const std::size_t smem = static_cast<std::size_t>(ex.world) * p.rows_per_cta * (ex.head_dim + 2) * 4;
         if (smem > 200 * 1024) throw std::runtime_error("peer exchange rows do not fit a CTA");
+        // Steps count from 1 (the zeroed words carry step 0); a wrap skips 0.
+        // The step is taken only once the call can launch, so a rejected call
+        // leaves this rank's count in step with its peers'.
+        if (++ex.step == 0) ex.step = 1;
+        p.step = ex.step;
         ilb::cuda_check(cudaFuncSetAttribute(ilb::peer_exchange_kernel,
                                              cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)),
                         "cudaFuncSetAttribute");

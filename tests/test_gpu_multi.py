@@ -6,7 +6,8 @@ partials, the partials are all-gathered over NCCL and merged in rank order;
 the result must equal the whole-context decode on one GPU within the fp32
 tolerance |a - b| <= 1e-6 + 1e-5 |b|. The decode with the exchange fused
 into it over NVLink peer memory (distributed.PeerExchange, five steps in a
-row so both buffer parities are reused), and then the packed partials
+row so both buffer parities are reused, with a call rejected on one rank
+between them that must leave the ranks' step counts in step), and then the packed partials
 through the standalone exchange kernel, must equal the NCCL result bit for
 bit. Ranks are spawned processes with a short process-group timeout.
 """
@@ -30,7 +31,7 @@ def _rank_main(rank, world, port, path):
     import torch
     import torch.distributed as dist
 
-    from inferlab_b200 import distributed, workloads as wl
+    from inferlab_b200 import distributed, paged, workloads as wl
 
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
@@ -48,12 +49,27 @@ def _rank_main(rank, world, port, path):
         blocks = full.block_tables[:, lo // 16:(hi + 15) // 16].contiguous()
         merged = distributed.decode_split_sequence(full.pool, full.queries, blocks, hi - lo)
         exchange = distributed.PeerExchange(32, 128)
-        # the decode and the exchange in one kernel, five steps in a row
-        peer = [distributed.decode_split_sequence(full.pool, full.queries, blocks, hi - lo,
-                                                  exchange=exchange).clone() for _ in range(5)]
+        lens = torch.full((1,), hi - lo, dtype=torch.int32, device=f"cuda:{rank}")
+
+        def fused():
+            return distributed.decode_split_sequence(full.pool, full.queries, blocks, hi - lo,
+                                                     exchange=exchange).clone()
+
+        # the decode and the exchange in one kernel, five steps in a row; after
+        # the second, rank 0 alone makes a call that is rejected (no split
+        # workspace): it must take no exchange step, or the ranks' later
+        # exchanges no longer pair up and their waits time out
+        peer = [fused() for _ in range(2)]
+        if rank == 0:
+            try:
+                exchange.decode(full.pool, full.queries, blocks, lens, hi - lo)
+            except paged.AttentionError as e:
+                assert "workspace is too small" in str(e), e
+            else:
+                raise AssertionError("a decode exchange without workspace was accepted")
+        peer += [fused() for _ in range(3)]
         # then the packed partials through the standalone exchange kernel
         send = torch.empty(32 * 130, dtype=torch.float32, device=f"cuda:{rank}")
-        lens = torch.full((1,), hi - lo, dtype=torch.int32, device=f"cuda:{rank}")
         for _ in range(2):
             full.pool.decode_partials(full.queries, blocks, lens, hi - lo, packed=send)
             peer.append(exchange.combine(send).view(1, 32, 128).clone())
