@@ -73,8 +73,10 @@ class PeerExchange:
     in one kernel over NVLink peer memory (inferlab_cuda_peer_exchange_*): each
     rank's receive buffer is opened by its peers through CUDA IPC handles swapped
     over the process group once; per call the kernel stores this rank's block
-    into every peer's buffer, raises that step's flag there, waits (bounded) for
-    all ranks' flags and merges. One process per GPU, every rank on its own GPU
+    into every peer's buffer as 8-byte words tagged with the call's step number,
+    waits (bounded) until every rank's words carry that step and merges. The
+    fused form (`decode`) does the same from inside the decode kernel. One
+    process per GPU, every rank on its own GPU
     (ranks sharing a GPU would wait on each other from separate launches), and
     every rank makes the same sequence of calls. Setting up is collective and
     agreed: if any rank cannot allocate or open a buffer, every rank raises
