@@ -559,7 +559,9 @@ void inferlab_cuda_peer_exchange_destroy(InferlabCudaPeerExchange* exchange);
  * rows from all ranks and merges them in rank order into out [num_seqs *
  * q_heads][head_dim] - the same bits as partials + exchange_combine. Takes
  * one step of `exchange`, like inferlab_cuda_peer_exchange_combine; a rank
- * with no blocks of the sequence calls that instead with an empty block.
+ * with no blocks of the sequence calls that instead with an empty block. A
+ * call rejected with an error (argument checks, workspace size, batch size)
+ * takes no step, so the ranks' later calls still pair up.
  * Needs the fast decode kernel's pool geometry, and at most half of the
  * GPU's resident decode CTAs may wait at once (num_seqs * kv_heads).
  */
