@@ -513,7 +513,10 @@ int inferlab_cuda_pages_copy(InferlabCudaKvPool* pool, const int32_t* from, cons
  * between two slots by step parity, so a rank one step ahead never overwrites
  * a block a peer is still reading. A wait that gives up records "device wait
  * timed out", read by inferlab_cuda_peer_exchange_synchronize.
- * Every rank must call the same sequence of exchanges; no reference
+ * Every rank must call the same sequence of exchanges, and each rank's
+ * exchanges must run one after another on the GPU (one stream, or streams
+ * ordered by events): the parity argument above holds only when a rank's
+ * exchange s + 2 starts after its exchange s + 1 has finished. No reference
  * counterpart (the reference has no split-sequence decode).
  */
 typedef struct InferlabCudaPeerExchange InferlabCudaPeerExchange;

@@ -77,8 +77,9 @@ class PeerExchange:
     waits (bounded) until every rank's words carry that step and merges. The
     fused form (`decode`) does the same from inside the decode kernel. One
     process per GPU, every rank on its own GPU
-    (ranks sharing a GPU would wait on each other from separate launches), and
-    every rank makes the same sequence of calls. Setting up is collective and
+    (ranks sharing a GPU would wait on each other from separate launches),
+    every rank makes the same sequence of calls, and a rank's calls run in
+    order on the GPU (one stream, or streams ordered by events). Setting up is collective and
     agreed: if any rank cannot allocate or open a buffer, every rank raises
     RuntimeError (and holds nothing), so callers can fall back together."""
 
