@@ -76,12 +76,12 @@ class PeerExchange:
     into every peer's buffer as 8-byte words tagged with the call's step number,
     waits (bounded) until every rank's words carry that step and merges. The
     fused form (`decode`) does the same from inside the decode kernel. One
-    process per GPU, every rank on its own GPU
-    (ranks sharing a GPU would wait on each other from separate launches),
-    every rank makes the same sequence of calls, and a rank's calls run in
-    order on the GPU (one stream, or streams ordered by events). Setting up is collective and
-    agreed: if any rank cannot allocate or open a buffer, every rank raises
-    RuntimeError (and holds nothing), so callers can fall back together."""
+    process per GPU, every rank on its own GPU (ranks sharing a GPU would wait
+    on each other from separate launches), every rank makes the same sequence
+    of calls, and a rank's calls run in order on the GPU (one stream, or
+    streams ordered by events). Setting up is collective and agreed: if any
+    rank cannot allocate or open a buffer, every rank raises RuntimeError (and
+    holds nothing), so callers can fall back together."""
 
     def __init__(self, rows: int, head_dim: int, group=None):
         import ctypes
