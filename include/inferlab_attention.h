@@ -534,7 +534,11 @@ int inferlab_cuda_peer_buffer_alloc(int device, uint64_t bytes, void** buffer, v
 int inferlab_cuda_peer_buffer_free(int device, void* buffer, char* error, size_t error_capacity);
 
 /* handles: world x INFERLAB_CUDA_IPC_HANDLE_BYTES, rank r's at r (this rank's
- * own entry is ignored); local_buffer: this rank's buffer. */
+ * own entry is ignored); local_buffer: this rank's buffer. Each exchange
+ * counts its steps from 1 and the buffers keep the last step-tagged words, so
+ * every exchange needs buffers fresh from inferlab_cuda_peer_buffer_alloc
+ * (zeroed): an exchange created again on buffers an earlier one used could
+ * take that one's words for its own. */
 int inferlab_cuda_peer_exchange_create(int device, uint32_t world, uint32_t rank, uint64_t rows,
                                        uint32_t head_dim, void* local_buffer, const void* handles,
                                        InferlabCudaPeerExchange** out, char* error,
